@@ -1,0 +1,54 @@
+"""Loader for the committed golden fixtures (tests/golden/*.pt) and a helper that
+replays one case through the CPU oracle."""
+
+import glob
+import os
+
+import torch
+
+from oracle import delrec_oracle as O
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def case_names():
+    return sorted(os.path.basename(p)[:-3] for p in glob.glob(os.path.join(GOLDEN, "*.pt"))
+                  if not os.path.basename(p).startswith("hybrid_dd"))
+
+
+def load(name):
+    return torch.load(os.path.join(GOLDEN, name + ".pt"), weights_only=False)
+
+
+def surrogate(meta):
+    return O.ATanSpike(2.0) if meta["surr"] == "atan" else O.TriangleSpike(1.0)
+
+
+def oracle_run(case, dtype=torch.float32):
+    """Forward + BPTT of one golden case through the oracle; returns a dict like the
+    fixture's ``v2`` entry."""
+    meta, inp = case["meta"], case["inputs"]
+    c = lambda t: None if t is None else t.to(dtype).clone()
+    x = c(inp["x"]).requires_grad_(True)
+    W = c(inp["W"]).requires_grad_(True)
+    base = c(inp["d"]).requires_grad_(True)
+    p = c(inp["p"]).requires_grad_(meta["use_sig_p"])
+    b = c(inp["bias"])
+    if b is not None:
+        b.requires_grad_(True)
+    lif = O.OracleLIF(tau=meta["tau"], v_threshold=1.0, v_reset=meta["v_reset"],
+                      surrogate=surrogate(meta), detach_reset=meta["detach_reset"])
+    kw = dict(sigma=meta["sigma"], p_spread=p, use_sig_p=meta["use_sig_p"], bias=b,
+              keep=c(inp["keep"]), record_u=True)
+    if meta["kind"] == "axonal":
+        y, u = O.axonal_scan(x, W, base, lif, **kw)
+    else:
+        d = O.hybrid_delays(base, c(inp["offsets"])) if meta["kind"] == "hybrid" else base
+        y, u = O.synaptic_scan(x, W, d, lif, **kw)
+    (y * c(inp["gy"])).sum().backward()
+    out = dict(y=y.detach(), u=u.detach(), dx=x.grad, dW=W.grad, dd=base.grad)
+    if meta["use_sig_p"]:
+        out["dp"] = p.grad
+    if b is not None:
+        out["dbias"] = b.grad
+    return out
