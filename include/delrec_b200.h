@@ -1,0 +1,190 @@
+/*
+ * delrec_b200: C-ABI of the B200-native delay-LIF hot path (DelRec).
+ *
+ * All pointers are device pointers, tensors are fp32, contiguous, time-major (T,B,N).
+ * Weights follow the reference's convention W[i,o] (row = target neuron i, column =
+ * source neuron o): rec[b,i] = sum_o W[i,o] * (delayed spike of o).
+ * Every entry point launches on `stream` (a cudaStream_t; NULL = legacy default stream),
+ * allocates nothing, and returns DELREC_OK or an error code.  Scratch memory is passed
+ * in by the caller: query its size with the matching *_workspace function.
+ *
+ * Reference interfaces replaced (paths are inside ZiyadBekrar/SNN-delays):
+ *   delrec_build_mask             triton_kernels/delays.py:13-29, 48-63 (build_mask,
+ *                                 build_syn_mask)
+ *   delrec_axonal_forward         triton_kernels/recdel_base.py:136-182 (recdel_triton_forward,
+ *                                 launching recdel_fwd_kernel :34-129)
+ *   delrec_axonal_backward        recdel_base.py:288-342 (recdel_triton_backward: recdel_bwd_kernel
+ *                                 :189-285 + host dW/db/dmask) and the dmask->dd/dp autograd
+ *                                 of AxonalRecdelTriton.backward :402-439
+ *   delrec_synaptic_forward       triton_kernels/synaptic_eventdriven.py:386-416 (EventDrivenSyn
+ *                                 .forward launching _ed_scatter_compact_kernel :106-164)
+ *   delrec_synaptic_backward      synaptic_eventdriven.py:419-471 (EventDrivenSyn.backward:
+ *                                 _ed_bwd_kernel :323-364 + Cstack GEMMs + autograd dd/dp)
+ *   delrec_hybrid_forward         triton_kernels/synaptic_hybrid.py:139-172 (HybridSynDelay.forward)
+ *   delrec_hybrid_backward        synaptic_hybrid.py:175-211 (HybridSynDelay.backward incl.
+ *                                 _hybrid_dd_kernel :83-113), with the (N,N) delay gradient
+ *                                 already reduced onto the learned (N,) base the way the
+ *                                 parametrization networks.py:823-829 does
+ *   delrec_hybrid_delay_grad      synaptic_hybrid.py:116-126 (_delay_grad, closed-form dd)
+ *   delrec_lif_forward/backward   the multi-step SpikingJelly LIFNode used between layers by
+ *                                 the model zoo (networks.py:84-96), no recurrence
+ *   delrec_dcls_forward/backward  networks.py:43-50 (dcls_module.forward: DCLS 0.1.1 Gaussian
+ *                                 kernel construction + causal conv1d over time)
+ */
+#ifndef DELREC_B200_H
+#define DELREC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------------- */
+#define DELREC_OK 0
+#define DELREC_ERR_ARG 1          /* invalid size / null pointer / bad enum            */
+#define DELREC_ERR_CUDA 2         /* a CUDA launch or attribute call failed             */
+#define DELREC_ERR_WORKSPACE 3    /* workspace too small or misaligned (256 B)          */
+#define DELREC_ERR_UNSUPPORTED 4  /* shape outside the kernels' supported range          */
+
+/* ---- delay kinds ------------------------------------------------------------------ */
+#define DELREC_AXONAL 0           /* d (N,): one delay per source neuron                */
+#define DELREC_SYNAPTIC 1         /* d (N,N): one delay per connection d[i,o]           */
+#define DELREC_HYBRID 2           /* learned base (N,) + frozen integer offsets (N,N)   */
+
+/* surrogate ids: identical to triton_kernels/surrogate.py:_SURR_ID */
+#define DELREC_SURR_TRIANGLE 0
+#define DELREC_SURR_ATAN 1
+
+/* LIF neuron, SpikingJelly LIFNode semantics with decay_input=False
+ * (charge v*(1-1/tau)+a when v_reset is None or 0, else v-(v-v_reset)/tau+a; fire
+ * u-v_th >= 0; hard reset to v_reset or soft reset by v_th; initial v = v_reset, or 0
+ * for a soft reset). */
+typedef struct delrec_lif {
+  float tau;
+  float v_threshold;
+  float v_reset;        /* ignored when soft_reset != 0 */
+  int32_t soft_reset;   /* 1: v_reset is None */
+  int32_t detach_reset; /* 1: no gradient through the reset */
+  int32_t surrogate;    /* DELREC_SURR_* */
+  float gamma;          /* Triangle width */
+  float alpha;          /* ATan slope */
+} delrec_lif;
+
+/* Shape and delay description of one recurrent delay layer. */
+typedef struct delrec_layer {
+  int32_t kind;         /* DELREC_AXONAL / DELREC_SYNAPTIC / DELREC_HYBRID */
+  int32_t T, B, N;
+  int32_t L;            /* ring length ceil(1 + max d + max s) + 1 (lags 1..L-1) */
+  int32_t K;            /* hybrid: largest integer offset (offsets in [0, K]) */
+  int32_t has_bias;     /* bias pointer is read */
+  int32_t has_keep;     /* keep (B,N) dropout mask is read */
+  float s_max;          /* largest triangle half-width (1 + sigma, or max over s) */
+  float d_min;          /* smallest delay (hybrid: smallest learned base; may be negative) */
+} delrec_layer;
+
+/* Gradient outputs of a layer backward.  Any pointer may be NULL to skip it. */
+typedef struct delrec_grads {
+  float* dx;            /* (T,B,N) */
+  float* dW;            /* (N,N)   */
+  float* dbias;         /* (N,)    */
+  float* dd;            /* axonal (N,), synaptic (N,N), hybrid base (N,) */
+  float* ds;            /* (N,) gradient w.r.t. the per-source half-width s (use_sig_p) */
+} delrec_grads;
+
+/* Triangle delay kernel h[r,l] = max(0, s_r' - |l - (1 + d[r])|) / s_r'^2 for l in [0,L),
+ * rows r in [0,R); s_r' = s[r % s_period] (s_period = N for synaptic (N,N) delays whose
+ * width is indexed by the source, = R for axonal).  out (R, L). */
+int delrec_build_mask(int R, int L, const float* d, const float* s, int s_period,
+                      float* out, void* stream);
+
+/* ---- axonal layer ------------------------------------------------------------------ */
+/* x (T,B,N), W (N,N), bias (N), d (N), s (N) half-widths, keep (B,N).
+ * Outputs y (spikes) and u (pre-reset membrane), both (T,B,N). */
+size_t delrec_axonal_forward_workspace(const delrec_layer* layer);
+int delrec_axonal_forward(const delrec_layer* layer, const delrec_lif* lif,
+                          const float* x, const float* W, const float* bias,
+                          const float* d, const float* s, const float* keep,
+                          float* y, float* u, void* workspace, size_t workspace_bytes,
+                          void* stream);
+/* gy (T,B,N) upstream gradient of the spikes; u, y from the forward. */
+size_t delrec_axonal_backward_workspace(const delrec_layer* layer);
+int delrec_axonal_backward(const delrec_layer* layer, const delrec_lif* lif,
+                           const float* gy, const float* u, const float* y,
+                           const float* W, const float* d, const float* s,
+                           const float* keep, const delrec_grads* grads,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- synaptic layer ---------------------------------------------------------------- */
+/* d (N,N) per connection, s (N) per source. */
+size_t delrec_synaptic_forward_workspace(const delrec_layer* layer);
+int delrec_synaptic_forward(const delrec_layer* layer, const delrec_lif* lif,
+                            const float* x, const float* W, const float* bias,
+                            const float* d, const float* s, const float* keep,
+                            float* y, float* u, void* workspace, size_t workspace_bytes,
+                            void* stream);
+size_t delrec_synaptic_backward_workspace(const delrec_layer* layer);
+int delrec_synaptic_backward(const delrec_layer* layer, const delrec_lif* lif,
+                             const float* gy, const float* u, const float* y,
+                             const float* W, const float* d, const float* s,
+                             const float* keep, const delrec_grads* grads,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- hybrid layer ------------------------------------------------------------------ */
+/* base (N,) learned per source, offsets (N,N) frozen integers in [0,K] (fp32, as the
+ * reference buffer); effective delay d[i,o] = base[o] + offsets[i,o].  s (N). */
+size_t delrec_hybrid_forward_workspace(const delrec_layer* layer);
+int delrec_hybrid_forward(const delrec_layer* layer, const delrec_lif* lif,
+                          const float* x, const float* W, const float* bias,
+                          const float* base, const float* offsets, const float* s,
+                          const float* keep, float* y, float* u,
+                          void* workspace, size_t workspace_bytes, void* stream);
+size_t delrec_hybrid_backward_workspace(const delrec_layer* layer);
+int delrec_hybrid_backward(const delrec_layer* layer, const delrec_lif* lif,
+                           const float* gy, const float* u, const float* y,
+                           const float* W, const float* base, const float* offsets,
+                           const float* s, const float* keep, const delrec_grads* grads,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* Closed-form per-synapse delay gradient of the hybrid/synaptic triangle kernel:
+ * dd[i,o] = W[i,o] * sum_{l=1}^{LM-1} C[i,o,l] * g(l - 1 - d[i,o]),
+ * g(a) = sign(a)/s^2 where |a| <= s, else 0  (s = 1 + sigma).  C (N,N,LM). */
+int delrec_hybrid_delay_grad(int N, int LM, const float* C, const float* W,
+                             const float* d, float sigma, float* dd, void* stream);
+
+/* ---- plain multi-step LIF (no recurrence) ------------------------------------------ */
+int delrec_lif_forward(int T, int M, const delrec_lif* lif, const float* x,
+                       float* y, float* u, void* stream);
+int delrec_lif_backward(int T, int M, const delrec_lif* lif, const float* gy,
+                        const float* u, float* dx, void* stream);
+
+/* ---- DCLS feedforward delay (Gaussian-interpolated positions, causal conv) ---------- */
+/* x (T,B,Cin); weight (Cout, Cin/groups); P, SIG (Cout, Cin/groups); kernel width K;
+ * left zero padding lpad (= K-1 for the causal length-preserving layer).  out (T,B,Cout).
+ * The constructed dense kernel is written to ker (Cout, Cin/groups, K). */
+int delrec_dcls_forward(int T, int B, int Cin, int Cout, int groups, int K, int lpad,
+                        const float* x, const float* weight, const float* P,
+                        const float* SIG, const float* bias, float* ker, float* out,
+                        void* stream);
+/* Gradients w.r.t. x, weight, P, SIG, bias (any may be NULL).  gout (T,B,Cout). */
+size_t delrec_dcls_backward_workspace(int T, int B, int Cin, int Cout, int groups, int K);
+int delrec_dcls_backward(int T, int B, int Cin, int Cout, int groups, int K, int lpad,
+                         const float* x, const float* weight, const float* P,
+                         const float* SIG, const float* gout, float* dx, float* dweight,
+                         float* dP, float* dSIG, float* dbias,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- device status word ------------------------------------------------------------ */
+/* Kernels record internal inconsistencies (an out-of-range lag or index that was
+ * skipped) in a device status word instead of trapping.  Reading it synchronizes. */
+int delrec_get_status(int* status_out);
+int delrec_clear_status(void);
+const char* delrec_version(void);
+/* Number of kernels this library has launched in this process (host-side counter). */
+unsigned long long delrec_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DELREC_B200_H */

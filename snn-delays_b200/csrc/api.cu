@@ -1,0 +1,692 @@
+// extern "C" entry points of libdelrec_b200.so: argument checks, workspace carving,
+// launch planning (block sizes, cluster shapes, shared-memory budgets) and the kernel
+// sequences of each layer forward / backward.  No allocation happens here: all
+// scratch comes from the caller's workspace.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+
+#include "backward.cuh"
+#include "forward.cuh"
+#include "grads.cuh"
+#include "misc.cuh"
+#include "prep.cuh"
+
+namespace delrec {
+
+static constexpr size_t kSmemLimit = 227 * 1024;  // opt-in dynamic shared memory per block
+static constexpr int kSMs = 148;
+static constexpr int kTapsMax = 16;               // widest axonal tap window supported
+
+static inline int pow2_at_least(int x) {
+  int r = 1;
+  while (r < x) r <<= 1;
+  return r;
+}
+
+#define DR_CUDA(call)                                                      \
+  do {                                                                     \
+    cudaError_t _e = (call);                                               \
+    if (_e != cudaSuccess) {                                               \
+      fprintf(stderr, "delrec_b200: %s failed: %s\n", #call, cudaGetErrorString(_e)); \
+      return DELREC_ERR_CUDA;                                              \
+    }                                                                      \
+  } while (0)
+static unsigned long long g_launches = 0;  // kernels issued by this library (host counter)
+
+#define DR_LAUNCHED()                                                      \
+  do {                                                                     \
+    ++g_launches;                                                          \
+    cudaError_t _e = cudaGetLastError();                                   \
+    if (_e != cudaSuccess) {                                               \
+      fprintf(stderr, "delrec_b200: launch failed at %s:%d: %s\n", __FILE__, __LINE__, \
+              cudaGetErrorString(_e));                                     \
+      return DELREC_ERR_CUDA;                                              \
+    }                                                                      \
+  } while (0)
+
+static inline int grid_for(size_t n, int threads) {
+  size_t g = (n + threads - 1) / threads;
+  if (g > (size_t)kSMs * 16) g = (size_t)kSMs * 16;
+  return (int)std::max<size_t>(g, 1);
+}
+
+// --------------------------------------------------------------------------------
+// layer descriptor validation
+// --------------------------------------------------------------------------------
+static int check_layer(const delrec_layer* ly, int kind) {
+  if (!ly || ly->kind != kind) return DELREC_ERR_ARG;
+  if (ly->T < 1 || ly->B < 1 || ly->N < 1 || ly->L < 1) return DELREC_ERR_ARG;
+  if (kind == DELREC_HYBRID && (ly->K < 0 || ly->K > 255)) return DELREC_ERR_ARG;
+  if (ly->N > 8192) return DELREC_ERR_UNSUPPORTED;
+  if (!(ly->s_max >= 1.f) || ly->s_max > 6.f) return DELREC_ERR_UNSUPPORTED;
+  return DELREC_OK;
+}
+
+// number of lags in an axonal tap window: [floor(1+d-s)-1, ceil(1+d+s)+1]
+static inline int taps_for(const delrec_layer* ly) {
+  const int w = 2 * (int)ceilf(ly->s_max) + 5;
+  // hybrid base windows may start below lag 1, so only the axonal window is capped by L-1
+  const int cap = ly->kind == DELREC_HYBRID ? w : std::min(ly->L - 1, w);
+  return std::max(1, std::min(cap, kTapsMax));
+}
+
+// Hybrid backward: the base's tap window may reach lags l <= 0 (a synapse with integer
+// offset k receives base lag l when l + k >= 1).  MM = 1 - (smallest such lag) over all
+// sources, evaluated with the device's float32 arithmetic on (min base, max width),
+// which bounds every source's window from below.  0 when every tap lag is >= 1.
+static int hybrid_mm(const delrec_layer* ly) {
+  const float onepd = 1.0f + ly->d_min;
+  const float s = ly->s_max;
+  int l = (int)floorf(onepd - s) - 1;
+  while (!(s - fabsf((float)l - onepd) >= 0.f) && l < 1) ++l;
+  int mm = 1 - l;
+  if (mm < 0) mm = 0;
+  if (mm > ly->K) mm = ly->K;
+  return mm;
+}
+static constexpr int kMMMax = 3;
+
+// --------------------------------------------------------------------------------
+// forward planning
+// --------------------------------------------------------------------------------
+struct FwdPlan {
+  int nth, ipt, R, NW, TAPS;
+  size_t smem;
+  int ring_smem;
+};
+
+static FwdPlan plan_forward(const delrec_layer* ly, int kind) {
+  FwdPlan p;
+  const int N = ly->N;
+  p.nth = std::min(512, ((N + 31) / 32) * 32);
+  p.ipt = cdiv(N, p.nth);
+  if (p.ipt > 2 && p.ipt <= 4) p.ipt = 4;
+  else if (p.ipt > 4) p.ipt = 8;
+  p.NW = cdiv(N, 32);
+  p.R = pow2_at_least(std::max(ly->L, 2));
+  p.TAPS = taps_for(ly);
+  if (kind == DELREC_AXONAL) {
+    p.ring_smem = 0;
+    p.smem = (size_t)p.R * p.NW * 4 + (size_t)N * (2 + p.TAPS) * 4 + (size_t)N * 8;
+  } else {
+    const size_t ring = (size_t)ly->L * N * 4;
+    p.ring_smem = (ring + (size_t)N * 4 <= 160 * 1024) ? 1 : 0;
+    p.smem = (p.ring_smem ? ring : 0) + (size_t)N * 4;
+  }
+  return p;
+}
+
+template <class K>
+static int set_smem(K kernel, size_t bytes) {
+  if (bytes > kSmemLimit) return DELREC_ERR_UNSUPPORTED;
+  DR_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+  return DELREC_OK;
+}
+
+template <int IPT>
+static int launch_fwd_axonal(const FwdArgs& a, const FwdPlan& p, cudaStream_t st) {
+  int rc = set_smem(k_fwd_axonal<IPT>, p.smem);
+  if (rc) return rc;
+  k_fwd_axonal<IPT><<<a.B, p.nth, p.smem, st>>>(a);
+  DR_LAUNCHED();
+  return DELREC_OK;
+}
+template <int IPT, bool HYB>
+static int launch_fwd_syn(const FwdArgs& a, const FwdPlan& p, cudaStream_t st) {
+  int rc = set_smem(k_fwd_synaptic<IPT, HYB>, p.smem);
+  if (rc) return rc;
+  k_fwd_synaptic<IPT, HYB><<<a.B, p.nth, p.smem, st>>>(a);
+  DR_LAUNCHED();
+  return DELREC_OK;
+}
+
+static size_t forward_ws(const delrec_layer* ly, int kind) {
+  const FwdPlan p = plan_forward(ly, kind);
+  const size_t N = ly->N;
+  Carve c(nullptr, (size_t)-1);
+  c.take<float>(N * N);                             // WT
+  if (kind == DELREC_AXONAL) {
+    c.take<int>(N); c.take<int>(N); c.take<float>(N * p.TAPS);
+  } else if (kind == DELREC_SYNAPTIC) {
+    c.take<float>(N * N);                           // dT
+  } else {
+    c.take<uint8_t>(N * N);                         // offT
+  }
+  if (kind != DELREC_AXONAL && !p.ring_smem) c.take<float>((size_t)ly->B * ly->L * N);
+  return c.off;
+}
+
+static int run_forward(const delrec_layer* ly, int kind, const delrec_lif* lif, const float* x,
+                       const float* W, const float* bias, const float* d, const float* offsets,
+                       const float* s, const float* keep, float* y, float* u, void* ws,
+                       size_t wsb, cudaStream_t st) {
+  int rc = check_layer(ly, kind);
+  if (rc) return rc;
+  if (!lif || !x || !W || !d || !s || !y || !u) return DELREC_ERR_ARG;
+  if (kind == DELREC_HYBRID && !offsets) return DELREC_ERR_ARG;
+  if (ly->has_bias && !bias) return DELREC_ERR_ARG;
+  if (ly->has_keep && !keep) return DELREC_ERR_ARG;
+  if (((uintptr_t)ws & 255) != 0) return DELREC_ERR_WORKSPACE;
+  if (wsb < forward_ws(ly, kind)) return DELREC_ERR_WORKSPACE;
+  const FwdPlan p = plan_forward(ly, kind);
+  const int N = ly->N;
+  Carve c(ws, wsb);
+  FwdArgs a{};
+  a.T = ly->T; a.B = ly->B; a.N = N; a.L = ly->L; a.R = p.R; a.NW = p.NW; a.TAPS = p.TAPS;
+  a.x = x; a.bias = ly->has_bias ? bias : nullptr; a.keep = ly->has_keep ? keep : nullptr; a.s = s;
+  a.y = y; a.u = u; a.lif = make_lif(*lif); a.ring_smem = p.ring_smem;
+  float* WT = c.take<float>((size_t)N * N);
+  dim3 tb(32, 8), tg(cdiv(N, 32), cdiv(N, 32));
+  k_transpose<<<tg, tb, 0, st>>>(W, WT, N, N);
+  DR_LAUNCHED();
+  a.WT = WT;
+  if (kind == DELREC_AXONAL) {
+    int* l0 = c.take<int>(N);
+    int* nt = c.take<int>(N);
+    float* w = c.take<float>((size_t)N * p.TAPS);
+    k_taps<<<cdiv(N, 256), 256, 0, st>>>(d, s, N, ly->L - 1, p.TAPS, 1, l0, nt, w);
+    DR_LAUNCHED();
+    a.tap_l0 = l0; a.tap_nt = nt; a.tap_w = w;
+    switch (p.ipt) {
+      case 1: return launch_fwd_axonal<1>(a, p, st);
+      case 2: return launch_fwd_axonal<2>(a, p, st);
+      case 4: return launch_fwd_axonal<4>(a, p, st);
+      default: return launch_fwd_axonal<8>(a, p, st);
+    }
+  }
+  if (kind == DELREC_SYNAPTIC) {
+    float* dT = c.take<float>((size_t)N * N);
+    k_transpose<<<tg, tb, 0, st>>>(d, dT, N, N);
+    DR_LAUNCHED();
+    a.dT = dT;
+  } else {
+    uint8_t* offT = c.take<uint8_t>((size_t)N * N);
+    k_offsets_u8T<<<tg, tb, 0, st>>>(offsets, offT, N, ly->K);
+    DR_LAUNCHED();
+    a.offT = offT;
+    a.base = d;
+  }
+  if (!p.ring_smem) a.ring_g = c.take<float>((size_t)ly->B * ly->L * N);
+  const bool hyb = kind == DELREC_HYBRID;
+  switch (p.ipt) {
+    case 1: return hyb ? launch_fwd_syn<1, true>(a, p, st) : launch_fwd_syn<1, false>(a, p, st);
+    case 2: return hyb ? launch_fwd_syn<2, true>(a, p, st) : launch_fwd_syn<2, false>(a, p, st);
+    case 4: return hyb ? launch_fwd_syn<4, true>(a, p, st) : launch_fwd_syn<4, false>(a, p, st);
+    default: return hyb ? launch_fwd_syn<8, true>(a, p, st) : launch_fwd_syn<8, false>(a, p, st);
+  }
+}
+
+// --------------------------------------------------------------------------------
+// backward planning
+// --------------------------------------------------------------------------------
+struct BwdPlan {
+  int mode, CS, NT, BT, KS, PPT, KH, NKEY, CAP, PADM, TAPS, w_smem, MM;
+  size_t smem;
+  bool ok;
+};
+
+static BwdPlan plan_backward(const delrec_layer* ly, int kind) {
+  const int N = ly->N, B = ly->B;
+  const int mode = kind == DELREC_AXONAL ? 0 : (kind == DELREC_HYBRID ? 1 : 2);
+  BwdPlan best{};
+  best.ok = false;
+  double best_cost = 1e300;
+  const int TAPS = taps_for(ly);
+  const int KH = ly->K + 1;
+  const int MM = mode == 1 ? hybrid_mm(ly) : 0;
+  const int bts[3] = {32, 16, 8};
+  const int css[5] = {1, 2, 4, 8, 16};
+  for (int bi = 0; bi < 3; ++bi) {
+    const int BT = bts[bi];
+    for (int ci = 0; ci < 5; ++ci) {
+      const int CS = css[ci];
+      int NT = ((cdiv(N, CS) + 3) / 4) * 4;
+      if (CS > 1 && (CS - 1) * NT >= N) continue;     // an empty rank
+      if (NT * BT > 1024) continue;                    // PPT <= 4 with 256 threads
+      const int tiles = (BT / 4) * (NT / 4);
+      if (mode == 0 && tiles > 256) continue;
+      const int KS = mode == 0 ? std::max(1, std::min(256 / tiles, N)) : 1;
+      int w_smem = 1;
+      BwdSmem sm = bwd_smem_plan(mode, N, NT, BT, KS, KH, ly->L, TAPS, w_smem, MM);
+      if (sm.total > kSmemLimit && mode == 0) {
+        w_smem = 0;
+        sm = bwd_smem_plan(mode, N, NT, BT, KS, KH, ly->L, TAPS, w_smem, MM);
+      }
+      if (sm.total > kSmemLimit) continue;
+      const int ctas = CS * cdiv(B, BT);
+      const int per_wave = (kSMs / CS) * CS;
+      const int waves = cdiv(ctas, per_wave);
+      // per-step work of one block (synapse-sample products) plus a cluster overhead
+      const double work = (double)NT * BT * (N + 64) * (mode == 0 ? 1.0 : 2.0) * (w_smem ? 1.0 : 2.0);
+      const double cost = waves * (work + 4000.0 * CS + 20000.0);
+      if (cost < best_cost) {
+        best_cost = cost;
+        best.ok = true;
+        best.mode = mode; best.CS = CS; best.NT = NT; best.BT = BT; best.KS = KS;
+        best.PPT = cdiv(NT * BT, 256); best.KH = KH; best.TAPS = TAPS; best.w_smem = w_smem;
+        best.MM = MM;
+        best.smem = sm.total;
+      }
+    }
+  }
+  best.NKEY = mode == 1 ? KH : ly->L;
+  best.PADM = best.ok ? 4 * (32 / best.BT) : 4;
+  best.CAP = (mode == 1 ? N : N * std::min(ly->L, 2 * kTapsMax)) + best.NKEY * best.PADM;
+  return best;
+}
+
+template <int MODE, int BT, int PPT>
+static int launch_bwd_t(const BwdArgs& a, const BwdPlan& p, cudaStream_t st) {
+  auto kern = k_bwd<MODE, BT, PPT>;
+  int rc = set_smem(kern, p.smem);
+  if (rc) return rc;
+  if (p.CS > 8) DR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.CS * cdiv(a.B, BT));
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.CS;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  DR_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
+  ++g_launches;
+  return DELREC_OK;
+}
+
+template <int MODE, int BT>
+static int launch_bwd_ppt(const BwdArgs& a, const BwdPlan& p, cudaStream_t st) {
+  switch (p.PPT) {
+    case 1: return launch_bwd_t<MODE, BT, 1>(a, p, st);
+    case 2: return launch_bwd_t<MODE, BT, 2>(a, p, st);
+    default: return launch_bwd_t<MODE, BT, 4>(a, p, st);
+  }
+}
+template <int MODE>
+static int launch_bwd_mode(const BwdArgs& a, const BwdPlan& p, cudaStream_t st) {
+  switch (p.BT) {
+    case 32: return launch_bwd_ppt<MODE, 32>(a, p, st);
+    case 16: return launch_bwd_ppt<MODE, 16>(a, p, st);
+    default: return launch_bwd_ppt<MODE, 8>(a, p, st);
+  }
+}
+
+// pair reduction planning
+struct PairPlan {
+  int KR, BCH, TW, splits, rows_per_split, NZ;
+  size_t smem;
+};
+static PairPlan plan_pairs(const delrec_layer* ly, int mode, const float* /*unused*/) {
+  PairPlan p;
+  p.NZ = mode == 1 ? hybrid_mm(ly) + 1 : 1;
+  const int N = ly->N;
+  int maxlag = 0;
+  if (mode == 1) maxlag = ly->K;
+  if (mode == 2) p.TW = std::min(std::max(std::min(ly->L - 1, 2 * (int)ceilf(ly->s_max) + 4), 1), 16);
+  else p.TW = 1;
+  if (mode == 2) maxlag = ly->L - 1 + 1;
+  p.KR = pow2_at_least(maxlag + p.TW + 1);
+  p.BCH = 32;
+  while (p.BCH > 8 && (size_t)(p.NZ * p.KR + 1) * p.BCH * 32 * 4 > 160 * 1024) p.BCH /= 2;
+  p.smem = (size_t)(p.NZ * p.KR + 1) * p.BCH * 32 * 4;
+  const int tiles = cdiv(N, 32) * cdiv(N, 32);
+  const int nbc = cdiv(ly->B, p.BCH);
+  int splits = std::max(1, std::min(nbc, cdiv(2 * kSMs, tiles)));
+  p.rows_per_split = cdiv(nbc, splits);
+  p.splits = cdiv(nbc, p.rows_per_split);
+  return p;
+}
+
+template <int MODE, int TW, int BCH>
+static int launch_pairs_t(const PairArgs& a, const PairPlan& p, int N, cudaStream_t st) {
+  auto kern = k_pair_reduce<MODE, TW, BCH>;
+  int rc = set_smem(kern, p.smem);
+  if (rc) return rc;
+  dim3 grid(cdiv(N, 32), cdiv(N, 32), p.splits);
+  kern<<<grid, 256, p.smem, st>>>(a);
+  DR_LAUNCHED();
+  return DELREC_OK;
+}
+template <int MODE, int TW>
+static int launch_pairs_b(const PairArgs& a, const PairPlan& p, int N, cudaStream_t st) {
+  switch (p.BCH) {
+    case 32: return launch_pairs_t<MODE, TW, 32>(a, p, N, st);
+    case 16: return launch_pairs_t<MODE, TW, 16>(a, p, N, st);
+    default: return launch_pairs_t<MODE, TW, 8>(a, p, N, st);
+  }
+}
+static int launch_pairs(int mode, const PairArgs& a, const PairPlan& p, int N, cudaStream_t st) {
+  if (mode == 0) return launch_pairs_b<0, 1>(a, p, N, st);
+  if (mode == 1) return launch_pairs_b<1, 1>(a, p, N, st);
+  if (p.TW <= 4) return launch_pairs_b<2, 4>(a, p, N, st);
+  if (p.TW <= 8) return launch_pairs_b<2, 8>(a, p, N, st);
+  return launch_pairs_b<2, 16>(a, p, N, st);
+}
+
+struct SrcPlan { int splits, rows_per_split; };
+static SrcPlan plan_src(const delrec_layer* ly) {
+  SrcPlan p;
+  const int TB = ly->T * ly->B;
+  const int cb = cdiv(ly->N, 32);
+  int splits = std::max(1, std::min(cdiv(2 * kSMs, cb), cdiv(TB, 256)));
+  p.rows_per_split = cdiv(TB, splits);
+  p.splits = cdiv(TB, p.rows_per_split);
+  return p;
+}
+
+static size_t backward_ws(const delrec_layer* ly, int kind) {
+  const BwdPlan bp = plan_backward(ly, kind);
+  const PairPlan pp = plan_pairs(ly, bp.mode, nullptr);
+  const SrcPlan sp = plan_src(ly);
+  const size_t N = ly->N, TBN = (size_t)ly->T * ly->B * N;
+  Carve c(nullptr, (size_t)-1);
+  c.take<float>(TBN);                                  // gr
+  if (kind != DELREC_SYNAPTIC) {
+    c.take<float>(TBN * (bp.MM + 1));                  // gz_m
+    c.take<float>(TBN * (bp.MM + 1));                  // z_m
+    c.take<int>(N); c.take<int>(N); c.take<float>(N * bp.TAPS);
+  }
+  if (kind == DELREC_HYBRID) c.take<uint8_t>(N * N);   // offT
+  if (kind == DELREC_SYNAPTIC) c.take<float>(N * N);   // dT
+  if (kind != DELREC_AXONAL) {
+    c.take<int2>(N * (size_t)bp.CAP);
+    c.take<int>(N * (size_t)(bp.NKEY + 1));
+  }
+  const int parts = kind == DELREC_SYNAPTIC ? 3 : 1;
+  c.take<float>((size_t)pp.splits * N * N * parts);   // pair partials
+  if (kind == DELREC_SYNAPTIC) c.take<float>(N * N);   // ds per pair, summed
+  c.take<float>((size_t)sp.splits * N * (bp.TAPS + 1)); // source partials
+  return c.off;
+}
+
+static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif, const float* gy,
+                        const float* u, const float* y, const float* W, const float* d,
+                        const float* offsets, const float* s, const float* keep,
+                        const delrec_grads* g, void* ws, size_t wsb, cudaStream_t st) {
+  int rc = check_layer(ly, kind);
+  if (rc) return rc;
+  if (!lif || !gy || !u || !y || !W || !d || !s || !g || !g->dx) return DELREC_ERR_ARG;
+  if (kind == DELREC_HYBRID && !offsets) return DELREC_ERR_ARG;
+  if (ly->has_keep && !keep) return DELREC_ERR_ARG;
+  if (((uintptr_t)ws & 255) != 0) return DELREC_ERR_WORKSPACE;
+  if (wsb < backward_ws(ly, kind)) return DELREC_ERR_WORKSPACE;
+  const BwdPlan bp = plan_backward(ly, kind);
+  if (!bp.ok || bp.MM > kMMMax) return DELREC_ERR_UNSUPPORTED;
+  const int N = ly->N, T = ly->T, B = ly->B;
+  const size_t TBN = (size_t)T * B * N;
+  Carve c(ws, wsb);
+  float* gr = c.take<float>(TBN);
+  float *gz = nullptr, *z = nullptr, *tw = nullptr;
+  int *tl0 = nullptr, *tnt = nullptr;
+  if (kind != DELREC_SYNAPTIC) {
+    gz = c.take<float>(TBN * (bp.MM + 1));
+    z = c.take<float>(TBN * (bp.MM + 1));
+    tl0 = c.take<int>(N);
+    tnt = c.take<int>(N);
+    tw = c.take<float>((size_t)N * bp.TAPS);
+    const int lmin = kind == DELREC_HYBRID ? 1 - ly->K : 1;
+    k_taps<<<cdiv(N, 256), 256, 0, st>>>(d, s, N, ly->L - 1, bp.TAPS, lmin, tl0, tnt, tw);
+    DR_LAUNCHED();
+  }
+  dim3 tb(32, 8), tg(cdiv(N, 32), cdiv(N, 32));
+  uint8_t* offT = nullptr;
+  float* dT = nullptr;
+  if (kind == DELREC_HYBRID) {
+    offT = c.take<uint8_t>((size_t)N * N);
+    k_offsets_u8T<<<tg, tb, 0, st>>>(offsets, offT, N, ly->K);
+    DR_LAUNCHED();
+  }
+  if (kind == DELREC_SYNAPTIC) {
+    dT = c.take<float>((size_t)N * N);
+    k_transpose<<<tg, tb, 0, st>>>(d, dT, N, N);
+    DR_LAUNCHED();
+  }
+  int2* ent = nullptr;
+  int* boff = nullptr;
+  if (kind != DELREC_AXONAL) {
+    ent = c.take<int2>((size_t)N * bp.CAP);
+    boff = c.take<int>((size_t)N * (bp.NKEY + 1));
+    const int nth = std::min(256, ((N + 31) / 32) * 32);
+    const size_t sm = (size_t)nth * 8;
+    if (kind == DELREC_HYBRID)
+      k_buckets<1><<<N, nth, sm, st>>>(N, bp.NKEY, bp.CAP, bp.PADM, W, offT, nullptr, s, ent, boff);
+    else
+      k_buckets<2><<<N, nth, sm, st>>>(N, bp.NKEY, bp.CAP, bp.PADM, W, nullptr, dT, s, ent, boff);
+    DR_LAUNCHED();
+  }
+  // ---- reverse scan
+  BwdArgs a{};
+  a.T = T; a.B = B; a.N = N; a.L = ly->L; a.KH = bp.KH; a.CS = bp.CS; a.NT = bp.NT;
+  a.TAPS = bp.TAPS; a.NKEY = bp.NKEY; a.CAP = bp.CAP; a.KS = bp.KS; a.MM = bp.MM;
+  a.gy = gy; a.u = u; a.keep = ly->has_keep ? keep : nullptr; a.W = W;
+  a.tap_l0 = tl0; a.tap_nt = tnt; a.tap_w = tw; a.ent = ent; a.boff = boff;
+  a.dx = g->dx; a.gr = gr; a.gz = gz; a.w_smem = bp.w_smem; a.lif = make_lif(*lif);
+  if (bp.mode == 0) rc = launch_bwd_mode<0>(a, bp, st);
+  else if (bp.mode == 1) rc = launch_bwd_mode<1>(a, bp, st);
+  else rc = launch_bwd_mode<2>(a, bp, st);
+  if (rc) return rc;
+  // ---- parameter gradients
+  const PairPlan pp = plan_pairs(ly, bp.mode, nullptr);
+  const int parts = kind == DELREC_SYNAPTIC ? 3 : 1;
+  float* ppart = c.take<float>((size_t)pp.splits * N * N * parts);
+  float* dsm = kind == DELREC_SYNAPTIC ? c.take<float>((size_t)N * N) : nullptr;
+  const SrcPlan sp = plan_src(ly);
+  float* spart = c.take<float>((size_t)sp.splits * N * (bp.TAPS + 1));
+  if (kind != DELREC_SYNAPTIC) {
+    k_axonal_z<<<grid_for(TBN, 256), 256, 0, st>>>(T, B, N, bp.TAPS, bp.MM + 1, y, tl0, tnt, tw, z);
+    DR_LAUNCHED();
+  }
+  if (g->dW || (kind == DELREC_SYNAPTIC && (g->dd || g->ds))) {
+    PairArgs pa{};
+    pa.T = T; pa.B = B; pa.N = N; pa.KR = pp.KR; pa.BCH = pp.BCH; pa.rows_per_split = pp.rows_per_split;
+    pa.gr = gr; pa.Y = kind == DELREC_SYNAPTIC ? y : z; pa.offT = offT; pa.dT = dT; pa.s = s; pa.W = W;
+    pa.Lm1 = ly->L - 1;
+    pa.NZ = pp.NZ;
+    const size_t nn = (size_t)N * N;
+    pa.out_dW = ppart;
+    pa.out_dd = kind == DELREC_SYNAPTIC ? ppart + (size_t)pp.splits * nn : nullptr;
+    pa.out_ds = kind == DELREC_SYNAPTIC ? ppart + (size_t)2 * pp.splits * nn : nullptr;
+    rc = launch_pairs(bp.mode, pa, pp, N, st);
+    if (rc) return rc;
+    if (g->dW) {
+      k_sum_splits<<<grid_for(nn, 256), 256, 0, st>>>(pa.out_dW, pp.splits, nn, g->dW);
+      DR_LAUNCHED();
+    }
+    if (kind == DELREC_SYNAPTIC) {
+      if (g->dd) {
+        k_sum_splits<<<grid_for(nn, 256), 256, 0, st>>>(pa.out_dd, pp.splits, nn, g->dd);
+        DR_LAUNCHED();
+      }
+      if (g->ds) {
+        k_sum_splits<<<grid_for(nn, 256), 256, 0, st>>>(pa.out_ds, pp.splits, nn, dsm);
+        DR_LAUNCHED();
+        k_colsum<<<cdiv(N, 128), 128, 0, st>>>(dsm, N, N, g->ds);
+        DR_LAUNCHED();
+      }
+    }
+  }
+  // per-neuron sums: db (all kinds), dd/ds of the axonal / hybrid base
+  const bool need_src = g->dbias || (kind != DELREC_SYNAPTIC && (g->dd || g->ds));
+  if (need_src) {
+    SrcArgs sa{};
+    sa.T = T; sa.B = B; sa.N = N; sa.TAPS = bp.TAPS; sa.rows_per_split = sp.rows_per_split;
+    sa.gr = gr; sa.gz = kind != DELREC_SYNAPTIC ? gz : nullptr; sa.y = y; sa.tap_l0 = tl0; sa.tap_nt = tnt;
+    sa.part = spart;
+    sa.MM = bp.MM;
+    dim3 grid(cdiv(N, 32), sp.splits);
+    if (bp.TAPS <= 4) k_source_reduce<4><<<grid, 256, 0, st>>>(sa);
+    else if (bp.TAPS <= 8) k_source_reduce<8><<<grid, 256, 0, st>>>(sa);
+    else k_source_reduce<16><<<grid, 256, 0, st>>>(sa);
+    DR_LAUNCHED();
+    const bool src_dd = kind != DELREC_SYNAPTIC;
+    k_source_finalize<<<cdiv(N, 128), 128, 0, st>>>(N, bp.TAPS, sp.splits, spart, d, s, tl0, tnt,
+                                                     g->dbias, src_dd ? g->dd : nullptr,
+                                                     src_dd ? g->ds : nullptr);
+    DR_LAUNCHED();
+  }
+  return DELREC_OK;
+}
+
+}  // namespace delrec
+
+using namespace delrec;
+
+extern "C" {
+
+const char* delrec_version(void) { return "delrec_b200 0.1 (sm_100a)"; }
+
+unsigned long long delrec_launch_count(void) { return g_launches; }
+
+int delrec_get_status(int* out) {
+  if (!out) return DELREC_ERR_ARG;
+  DR_CUDA(cudaDeviceSynchronize());
+  DR_CUDA(cudaMemcpyFromSymbol(out, g_status, sizeof(int)));
+  return DELREC_OK;
+}
+int delrec_clear_status(void) {
+  const int z = 0;
+  DR_CUDA(cudaMemcpyToSymbol(g_status, &z, sizeof(int)));
+  return DELREC_OK;
+}
+
+int delrec_build_mask(int R, int L, const float* d, const float* s, int s_period, float* out, void* stream) {
+  if (R < 1 || L < 1 || s_period < 1 || !d || !s || !out) return DELREC_ERR_ARG;
+  k_build_mask<<<grid_for((size_t)R * L, 256), 256, 0, (cudaStream_t)stream>>>(R, L, d, s, s_period, out);
+  DR_LAUNCHED();
+  return DELREC_OK;
+}
+
+size_t delrec_axonal_forward_workspace(const delrec_layer* ly) { return ly ? forward_ws(ly, DELREC_AXONAL) : 0; }
+size_t delrec_synaptic_forward_workspace(const delrec_layer* ly) { return ly ? forward_ws(ly, DELREC_SYNAPTIC) : 0; }
+size_t delrec_hybrid_forward_workspace(const delrec_layer* ly) { return ly ? forward_ws(ly, DELREC_HYBRID) : 0; }
+size_t delrec_axonal_backward_workspace(const delrec_layer* ly) { return ly ? backward_ws(ly, DELREC_AXONAL) : 0; }
+size_t delrec_synaptic_backward_workspace(const delrec_layer* ly) { return ly ? backward_ws(ly, DELREC_SYNAPTIC) : 0; }
+size_t delrec_hybrid_backward_workspace(const delrec_layer* ly) { return ly ? backward_ws(ly, DELREC_HYBRID) : 0; }
+
+int delrec_axonal_forward(const delrec_layer* ly, const delrec_lif* lif, const float* x, const float* W,
+                          const float* bias, const float* d, const float* s, const float* keep, float* y,
+                          float* u, void* ws, size_t wsb, void* stream) {
+  return run_forward(ly, DELREC_AXONAL, lif, x, W, bias, d, nullptr, s, keep, y, u, ws, wsb, (cudaStream_t)stream);
+}
+int delrec_synaptic_forward(const delrec_layer* ly, const delrec_lif* lif, const float* x, const float* W,
+                            const float* bias, const float* d, const float* s, const float* keep, float* y,
+                            float* u, void* ws, size_t wsb, void* stream) {
+  return run_forward(ly, DELREC_SYNAPTIC, lif, x, W, bias, d, nullptr, s, keep, y, u, ws, wsb, (cudaStream_t)stream);
+}
+int delrec_hybrid_forward(const delrec_layer* ly, const delrec_lif* lif, const float* x, const float* W,
+                          const float* bias, const float* base, const float* offsets, const float* s,
+                          const float* keep, float* y, float* u, void* ws, size_t wsb, void* stream) {
+  return run_forward(ly, DELREC_HYBRID, lif, x, W, bias, base, offsets, s, keep, y, u, ws, wsb, (cudaStream_t)stream);
+}
+
+int delrec_axonal_backward(const delrec_layer* ly, const delrec_lif* lif, const float* gy, const float* u,
+                           const float* y, const float* W, const float* d, const float* s, const float* keep,
+                           const delrec_grads* g, void* ws, size_t wsb, void* stream) {
+  return run_backward(ly, DELREC_AXONAL, lif, gy, u, y, W, d, nullptr, s, keep, g, ws, wsb, (cudaStream_t)stream);
+}
+int delrec_synaptic_backward(const delrec_layer* ly, const delrec_lif* lif, const float* gy, const float* u,
+                             const float* y, const float* W, const float* d, const float* s, const float* keep,
+                             const delrec_grads* g, void* ws, size_t wsb, void* stream) {
+  return run_backward(ly, DELREC_SYNAPTIC, lif, gy, u, y, W, d, nullptr, s, keep, g, ws, wsb, (cudaStream_t)stream);
+}
+int delrec_hybrid_backward(const delrec_layer* ly, const delrec_lif* lif, const float* gy, const float* u,
+                           const float* y, const float* W, const float* base, const float* offsets,
+                           const float* s, const float* keep, const delrec_grads* g, void* ws, size_t wsb,
+                           void* stream) {
+  return run_backward(ly, DELREC_HYBRID, lif, gy, u, y, W, base, offsets, s, keep, g, ws, wsb, (cudaStream_t)stream);
+}
+
+int delrec_hybrid_delay_grad(int N, int LM, const float* C, const float* W, const float* d, float sigma,
+                             float* dd, void* stream) {
+  if (N < 1 || LM < 1 || !C || !W || !d || !dd) return DELREC_ERR_ARG;
+  k_hybrid_delay_grad<<<grid_for((size_t)N * N, 256), 256, 0, (cudaStream_t)stream>>>(N, LM, C, W, d, 1.f + sigma, dd);
+  DR_LAUNCHED();
+  return DELREC_OK;
+}
+
+int delrec_lif_forward(int T, int M, const delrec_lif* lif, const float* x, float* y, float* u, void* stream) {
+  if (T < 1 || M < 1 || !lif || !x || !y) return DELREC_ERR_ARG;
+  k_lif_fwd<<<cdiv(M, 256), 256, 0, (cudaStream_t)stream>>>(T, M, make_lif(*lif), x, y, u);
+  DR_LAUNCHED();
+  return DELREC_OK;
+}
+int delrec_lif_backward(int T, int M, const delrec_lif* lif, const float* gy, const float* u, float* dx,
+                        void* stream) {
+  if (T < 1 || M < 1 || !lif || !gy || !u || !dx) return DELREC_ERR_ARG;
+  k_lif_bwd<<<cdiv(M, 256), 256, 0, (cudaStream_t)stream>>>(T, M, make_lif(*lif), gy, u, dx);
+  DR_LAUNCHED();
+  return DELREC_OK;
+}
+
+static int dcls_check(int T, int B, int Cin, int Cout, int groups, int K, int lpad) {
+  if (T < 1 || B < 1 || Cin < 1 || Cout < 1 || groups < 1 || K < 1 || lpad < 0) return DELREC_ERR_ARG;
+  if (Cin % groups || Cout % groups) return DELREC_ERR_ARG;
+  if (K > 64) return DELREC_ERR_UNSUPPORTED;
+  return DELREC_OK;
+}
+
+int delrec_dcls_forward(int T, int B, int Cin, int Cout, int groups, int K, int lpad, const float* x,
+                        const float* weight, const float* P, const float* SIG, const float* bias, float* ker,
+                        float* out, void* stream) {
+  int rc = dcls_check(T, B, Cin, Cout, groups, K, lpad);
+  if (rc) return rc;
+  if (!x || !weight || !P || !SIG || !ker || !out) return DELREC_ERR_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int rows = Cout * (Cin / groups);
+  k_dcls_build<<<cdiv(rows, 128), 128, 0, st>>>(rows, K, weight, P, SIG, ker);
+  DR_LAUNCHED();
+  k_dcls_conv<<<grid_for((size_t)T * B * Cout, 256), 256, 0, st>>>(T, B, Cin, Cout, groups, K, lpad, x, ker, bias, out);
+  DR_LAUNCHED();
+  return DELREC_OK;
+}
+
+size_t delrec_dcls_backward_workspace(int T, int B, int Cin, int Cout, int groups, int K) {
+  (void)T; (void)B;
+  if (groups < 1) return 0;
+  Carve c(nullptr, (size_t)-1);
+  c.take<float>((size_t)Cout * (Cin / groups) * K);  // ker
+  c.take<float>((size_t)Cout * (Cin / groups) * K);  // dker
+  return c.off;
+}
+
+int delrec_dcls_backward(int T, int B, int Cin, int Cout, int groups, int K, int lpad, const float* x,
+                         const float* weight, const float* P, const float* SIG, const float* gout, float* dx,
+                         float* dweight, float* dP, float* dSIG, float* dbias, void* ws, size_t wsb,
+                         void* stream) {
+  int rc = dcls_check(T, B, Cin, Cout, groups, K, lpad);
+  if (rc) return rc;
+  if (!x || !weight || !P || !SIG || !gout) return DELREC_ERR_ARG;
+  if (((uintptr_t)ws & 255) != 0 || wsb < delrec_dcls_backward_workspace(T, B, Cin, Cout, groups, K))
+    return DELREC_ERR_WORKSPACE;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int rows = Cout * (Cin / groups);
+  Carve c(ws, wsb);
+  float* ker = c.take<float>((size_t)rows * K);
+  float* dker = c.take<float>((size_t)rows * K);
+  k_dcls_build<<<cdiv(rows, 128), 128, 0, st>>>(rows, K, weight, P, SIG, ker);
+  DR_LAUNCHED();
+  if (dx) {
+    k_dcls_dx<<<grid_for((size_t)T * B * Cin, 256), 256, 0, st>>>(T, B, Cin, Cout, groups, K, lpad, gout, ker, dx);
+    DR_LAUNCHED();
+  }
+  if (dweight || dP || dSIG) {
+    k_dcls_dker<<<rows * K, 256, 0, st>>>(T, B, Cin, Cout, groups, K, lpad, x, gout, dker);
+    DR_LAUNCHED();
+    k_dcls_params<<<cdiv(rows, 128), 128, 0, st>>>(rows, K, weight, P, SIG, dker, dweight, dP, dSIG);
+    DR_LAUNCHED();
+  }
+  if (dbias) {
+    k_dcls_dbias<<<cdiv(Cout, 128), 128, 0, st>>>(T * B, Cout, gout, dbias);
+    DR_LAUNCHED();
+  }
+  return DELREC_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,216 @@
+// Forward time scans.  One thread block owns one sample for all T steps and all N
+// neurons, so the recurrence never leaves the block; per step it
+//   * axonal:  gathers z_o = sum_l h_o(l) y[t-l,o] from a bit-packed spike history in
+//              shared memory, compacts the nonzero z into an event list, and accumulates
+//              rec_i = sum_events W[i,o] z_o in registers (spike-sparse: only sources with
+//              a spike inside their delay window cost anything);
+//   * synaptic / hybrid: reads rec from a delay ring (shared memory when it fits),
+//              runs the LIF update, compacts the neurons that fired, and scatters each
+//              fired source's W[:,o] * h(l; d_io) into the ring slots t+l of its targets.
+// Matches delrec/delay_layers_pytorch.py:121-194 (axonal v2) and :271-325 (synaptic
+// v2); the hybrid delay d[i,o] = base[o] + offsets[i,o] (networks.py:823-829) is formed
+// on the fly from a uint8 offset table.
+#pragma once
+
+#include "prep.cuh"
+
+namespace delrec {
+
+struct FwdArgs {
+  int T, B, N, L, R, NW, TAPS;
+  const float* x;
+  const float* WT;        // W transposed: WT[o*N + i] = W[i,o]
+  const float* bias;      // (N) or null
+  const float* keep;      // (B,N) or null
+  const float* s;         // (N) half-widths
+  const float* dT;        // synaptic: d transposed (N,N)
+  const uint8_t* offT;    // hybrid: offsets transposed (N,N)
+  const float* base;      // hybrid base (N)
+  const int* tap_l0;
+  const int* tap_nt;
+  const float* tap_w;
+  float* y;
+  float* u;
+  float* ring_g;          // global ring (B, L, N) when it does not fit in shared memory
+  int ring_smem;
+  LifK lif;
+};
+
+// --------------------------------------------------------------------------------
+// axonal: z-gather + register accumulation.   dynamic smem:
+//   hist  R*NW u32 | l0 N int | nt N int | w N*TAPS f32 | ev_o N int | ev_z N f32
+// --------------------------------------------------------------------------------
+template <int IPT>
+__global__ void __launch_bounds__(512) k_fwd_axonal(FwdArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ int s_warp[33];
+  const int N = a.N, T = a.T, B = a.B, NTH = blockDim.x, tid = threadIdx.x;
+  const int b = blockIdx.x;
+  uint32_t* hist = (uint32_t*)smem;
+  int* sl0 = (int*)(hist + (size_t)a.R * a.NW);
+  int* snt = sl0 + N;
+  float* sw = (float*)(snt + N);
+  int* ev_o = (int*)(sw + (size_t)N * a.TAPS);
+  float* ev_z = (float*)(ev_o + N);
+
+  for (int e = tid; e < a.R * a.NW; e += NTH) hist[e] = 0u;
+  for (int o = tid; o < N; o += NTH) { sl0[o] = a.tap_l0[o]; snt[o] = a.tap_nt[o]; }
+  for (int e = tid; e < N * a.TAPS; e += NTH) sw[e] = a.tap_w[e];
+
+  float v[IPT], kp[IPT], bs[IPT];
+#pragma unroll
+  for (int q = 0; q < IPT; ++q) {
+    const int i = q * NTH + tid;
+    v[q] = a.lif.v0;
+    kp[q] = (a.keep && i < N) ? a.keep[(size_t)b * N + i] : 1.f;
+    bs[q] = (a.bias && i < N) ? a.bias[i] : 0.f;
+  }
+  __syncthreads();
+
+  const int rounds = cdiv(N, NTH);
+  for (int t = 0; t < T; ++t) {
+    // ---- z gather + compaction of the nonzero delayed inputs
+    int nev = 0;
+    for (int r = 0; r < rounds; ++r) {
+      const int o = r * NTH + tid;
+      float z = 0.f;
+      if (o < N) {
+        const int lo = sl0[o], n = snt[o];
+        const int word = o >> 5;
+        const uint32_t bit = 1u << (o & 31);
+        for (int j = 0; j < n; ++j) {
+          const int tt = t - lo - j;
+          if (tt >= 0 && (hist[(size_t)(tt & (a.R - 1)) * a.NW + word] & bit))
+            z = __fadd_rn(z, sw[(size_t)o * a.TAPS + j]);
+        }
+      }
+      nev += block_compact(z != 0.f, o, z, ev_o, ev_z, nev, s_warp);
+    }
+    // ---- rec_i = sum over events of W[i,o] * z_o
+    float acc[IPT];
+#pragma unroll
+    for (int q = 0; q < IPT; ++q) acc[q] = 0.f;
+#pragma unroll 4
+    for (int e = 0; e < nev; ++e) {
+      const int o = ev_o[e];
+      const float zv = ev_z[e];
+      const float* wrow = a.WT + (size_t)o * N;
+#pragma unroll
+      for (int q = 0; q < IPT; ++q) {
+        const int i = q * NTH + tid;
+        if (i < N) acc[q] = fmaf(__ldg(wrow + i), zv, acc[q]);
+      }
+    }
+    // ---- LIF, outputs, spike bits
+    const size_t rowoff = ((size_t)t * B + b) * N;
+#pragma unroll
+    for (int q = 0; q < IPT; ++q) {
+      const int i = q * NTH + tid;
+      bool sp = false;
+      if (i < N) {
+        const float rec = __fmul_rn(__fadd_rn(acc[q], bs[q]), kp[q]);
+        const float av = __fadd_rn(a.x[rowoff + i], rec);
+        const float uu = lif_charge(v[q], av, a.lif);
+        sp = lif_fire(uu, a.lif);
+        v[q] = lif_reset(uu, sp, a.lif);
+        a.y[rowoff + i] = sp ? 1.f : 0.f;
+        a.u[rowoff + i] = uu;
+      }
+      const unsigned m = __ballot_sync(0xffffffffu, sp);
+      const int word = (q * NTH + (tid & ~31)) >> 5;
+      if ((tid & 31) == 0 && word < a.NW) hist[(size_t)(t & (a.R - 1)) * a.NW + word] = m;
+    }
+    __syncthreads();
+  }
+}
+
+// --------------------------------------------------------------------------------
+// synaptic / hybrid: delay ring + spike-event scatter.   dynamic smem:
+//   ring L*N f32 (if ring_smem) | ev_o N int
+// --------------------------------------------------------------------------------
+template <int IPT, bool HYB>
+__global__ void __launch_bounds__(512) k_fwd_synaptic(FwdArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ int s_warp[33];
+  const int N = a.N, T = a.T, B = a.B, L = a.L, NTH = blockDim.x, tid = threadIdx.x;
+  const int b = blockIdx.x;
+  float* ring;
+  int* ev_o;
+  if (a.ring_smem) {
+    ring = (float*)smem;
+    ev_o = (int*)(ring + (size_t)L * N);
+  } else {
+    ring = a.ring_g + (size_t)b * L * N;
+    ev_o = (int*)smem;
+  }
+  for (size_t e = tid; e < (size_t)L * N; e += NTH) ring[e] = 0.f;
+
+  float v[IPT], kp[IPT], bs[IPT];
+#pragma unroll
+  for (int q = 0; q < IPT; ++q) {
+    const int i = q * NTH + tid;
+    v[q] = a.lif.v0;
+    kp[q] = (a.keep && i < N) ? a.keep[(size_t)b * N + i] : 1.f;
+    bs[q] = (a.bias && i < N) ? a.bias[i] : 0.f;
+  }
+  __syncthreads();
+
+  int slot = 0;  // t mod L
+  for (int t = 0; t < T; ++t) {
+    const size_t rowoff = ((size_t)t * B + b) * N;
+    int nev = 0;
+#pragma unroll
+    for (int q = 0; q < IPT; ++q) {
+      const int i = q * NTH + tid;
+      bool sp = false;
+      if (i < N) {
+        float* cell = ring + (size_t)slot * N + i;
+        const float rsum = *cell;
+        *cell = 0.f;
+        const float rec = __fmul_rn(__fadd_rn(rsum, bs[q]), kp[q]);
+        const float av = __fadd_rn(a.x[rowoff + i], rec);
+        const float uu = lif_charge(v[q], av, a.lif);
+        sp = lif_fire(uu, a.lif);
+        v[q] = lif_reset(uu, sp, a.lif);
+        a.y[rowoff + i] = sp ? 1.f : 0.f;
+        a.u[rowoff + i] = uu;
+      }
+      nev += block_compact(sp, i, 0.f, ev_o, nullptr, nev, s_warp);
+    }
+    // ---- scatter the fired sources into the ring (lags 1..L-1)
+    for (int e = 0; e < nev; ++e) {
+      const int o = ev_o[e];
+      const float so = a.s[o];
+      const float bo = HYB ? a.base[o] : 0.f;
+      const float* wrow = a.WT + (size_t)o * N;
+#pragma unroll
+      for (int q = 0; q < IPT; ++q) {
+        const int i = q * NTH + tid;
+        if (i >= N) continue;
+        const float w = __ldg(wrow + i);
+        const float d = HYB ? __fadd_rn(bo, (float)a.offT[(size_t)o * N + i]) : __ldg(a.dT + (size_t)o * N + i);
+        const Tri tr = make_tri(d, so);
+        int lo = (int)floorf(__fsub_rn(tr.onepd, tr.s));
+        int hi = (int)ceilf(__fadd_rn(tr.onepd, tr.s));
+        lo = lo < 1 ? 1 : lo;
+        if (hi > L - 1) {
+          if (tri_clamped(tr, L) > 0.f) flag_status(ST_LAG_RANGE);
+          hi = L - 1;
+        }
+        for (int l = lo; l <= hi; ++l) {
+          const float c = tri_clamped(tr, l);
+          if (c > 0.f) {
+            int sl = slot + l;
+            if (sl >= L) sl -= L;
+            float* cell = ring + (size_t)sl * N + i;
+            *cell = __fadd_rn(*cell, __fmul_rn(w, __fdiv_rn(c, tr.s2)));
+          }
+        }
+      }
+    }
+    __syncthreads();
+    slot = (slot + 1 == L) ? 0 : slot + 1;
+  }
+}
+
+}  // namespace delrec

@@ -1,0 +1,151 @@
+"""Module-level drop-in contract checked on CPU: constructors, parameter names and
+state_dict layout, the hybrid reparametrization, sigma annealing, the ValueError paths
+of the reference, and that a CPU forward raises instead of falling back."""
+
+import copy
+import math
+
+import pytest
+import torch
+
+from model_configs import mem_config
+
+
+def _nw():
+    from delrec import networks
+    return networks
+
+
+def test_axonal_state_dict_layout():
+    nw = _nw()
+    cfg = mem_config(hidden=[16], bias=False)
+    torch.manual_seed(0)
+    m = nw.SNN_axonal_recurrent_delays(cfg)
+    keys = set(m.state_dict())
+    assert keys == {"layers.0.weight", "layers.2.recurrent_weights", "layers.2.recurrent_delays",
+                    "layers.4.weight"}, keys
+    rec = m.layers[2]
+    assert rec.recurrent_weights.shape == (16, 16) and rec.recurrent_delays.shape == (16,)
+    assert isinstance(rec.sigma, float) and "sigma" not in m.state_dict()
+
+
+def test_optional_parameters():
+    nw = _nw()
+    cfg = mem_config(hidden=[8], bias=True)
+    cfg.use_sig_p = True
+    cfg.use_rec_bias = True
+    m = nw.SNN_synaptic_recurrent_delays(cfg)
+    keys = set(m.state_dict())
+    for k in ("layers.2.recurrent_weights", "layers.2.recurrent_delays", "layers.2.p_spread",
+              "layers.2.recurrent_bias", "layers.0.bias", "layers.4.bias"):
+        assert k in keys
+    assert m.layers[2].recurrent_delays.shape == (8, 8)
+
+
+@pytest.mark.parametrize("maximum", [0, 4])
+def test_hybrid_layout(maximum):
+    nw = _nw()
+    cfg = mem_config(hidden=[16], bias=False)
+    cfg.hybrid_offset_scale = maximum
+    torch.manual_seed(0)
+    h = nw.SNN_recurrent_hybrid_delays(cfg)
+    if maximum == 0:
+        torch.manual_seed(0)
+        a = nw.SNN_axonal_recurrent_delays(cfg)
+        hs, as_ = h.state_dict(), a.state_dict()
+        assert set(hs) == set(as_)
+        for k in as_:
+            assert torch.equal(hs[k], as_[k]), k
+        return
+    keys = set(h.state_dict())
+    assert "layers.2.parametrizations.recurrent_delays.original" in keys
+    assert "layers.2.parametrizations.recurrent_delays.0.offsets" in keys
+    leaf = nw.learned_delay_parameter(h.layers[2], "recurrent_delays")
+    assert leaf.shape == (16,) and leaf.requires_grad
+    off = h.layers[2].parametrizations.recurrent_delays[0].offsets
+    assert not off.requires_grad and off.min() >= 0 and off.max() <= maximum
+    assert torch.equal(off, off.round())
+    # the effective (N, N) delay is base[o] + offsets[i, o]
+    d = h.layers[2].recurrent_delays
+    assert torch.allclose(d, leaf[None, :] + off)
+    assert getattr(h.layers[2], "_hybrid_delay", False)
+
+
+def test_hybrid_offsets_follow_the_seeded_generator():
+    nw = _nw()
+    cfg = mem_config(hidden=[12], bias=False)
+    cfg.hybrid_offset_scale = 3
+    a = nw.SNN_recurrent_hybrid_delays(cfg)
+    b = nw.SNN_recurrent_hybrid_delays(cfg)
+    oa = a.layers[2].parametrizations.recurrent_delays[0].offsets
+    ob = b.layers[2].parametrizations.recurrent_delays[0].offsets
+    assert torch.equal(oa, ob)
+    g = torch.Generator().manual_seed(cfg.hybrid_delay_seed)
+    assert torch.equal(oa, torch.randint(4, (12, 12), generator=g).float())
+
+
+def test_value_errors():
+    nw = _nw()
+    for bad in (-1, 1.5):
+        cfg = mem_config(hidden=[8])
+        cfg.hybrid_offset_scale = bad
+        with pytest.raises(ValueError):
+            nw.SNN_recurrent_hybrid_delays(cfg)
+    cfg = mem_config(hidden=[8])
+    cfg.kernel_count = 2
+    with pytest.raises(ValueError):
+        nw.SNN_recurrent_hybrid_delays(cfg)
+
+
+def test_update_sigma_schedule():
+    nw = _nw()
+    cfg = mem_config(hidden=[8])
+    cfg.sigma_init, cfg.sigma_decay, cfg.epochs = 2.0, 0.95, 50
+    m = nw.SNN_axonal_recurrent_delays(cfg)
+    layer = m.layers[2]
+    layer.update_sigma(10)
+    assert math.isclose(layer.sigma, 2.0 * (0.95 ** (100 / 50)) ** 10)
+
+
+def test_clamp_and_round():
+    nw = _nw()
+    cfg = mem_config(hidden=[8])
+    cfg.hybrid_offset_scale = 2
+    m = nw.SNN_recurrent_hybrid_delays(cfg)
+    leaf = nw.learned_delay_parameter(m.layers[2], "recurrent_delays")
+    with torch.no_grad():
+        leaf.copy_(torch.linspace(-2, 3.4, 8))
+    m.round_pos()
+    assert torch.equal(leaf, leaf.round()) and leaf.min() >= 0
+
+
+def test_cpu_forward_raises_no_fallback():
+    nw = _nw()
+    cfg = mem_config(hidden=[8])
+    m = nw.SNN_axonal_recurrent_delays(cfg)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        m(torch.zeros(4, 2, cfg.input_size))
+
+
+def test_reference_forward_versions_are_not_shipped():
+    nw = _nw()
+    cfg = mem_config(hidden=[8])
+    m = nw.SNN_axonal_recurrent_delays(cfg)
+    m.layers[2].forward_version = "v2"
+    from delrec.delay_layers import _check_cuda
+    x = torch.zeros(2, 2, 8)
+    with pytest.raises(RuntimeError):
+        m(torch.zeros(4, 2, cfg.input_size))
+
+
+def test_feedforward_models_build():
+    nw = _nw()
+    cfg = mem_config(hidden=[16])
+    for name in ("SNN_axonal_feedforward_delays", "SNN_synaptic_feedforward_delays",
+                 "SNN_hybrid_feedforward_delays", "SNN_recurrent_and_feedforward_delays",
+                 "SNN_hybrid_recurrent_and_feedforward_delays"):
+        m = getattr(nw, name)(cfg)
+        assert sum(p.numel() for p in m.parameters()) > 0
+    h = nw.SNN_hybrid_feedforward_delays(cfg)
+    dc = [m for m in h.layers if isinstance(m, nw.dcls_module)][0]
+    assert nw.learned_delay_parameter(dc, "P").shape[:3] == (1, 1, cfg.input_size)
