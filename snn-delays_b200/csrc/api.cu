@@ -9,6 +9,7 @@
 #include <cstring>
 
 #include "backward.cuh"
+#include "backward_hybrid.cuh"
 #include "forward.cuh"
 #include "grads.cuh"
 #include "misc.cuh"
@@ -274,8 +275,54 @@ static BwdPlan plan_backward(const delrec_layer* ly, int kind) {
   }
   best.NKEY = mode == 1 ? KH : ly->L;
   best.PADM = best.ok ? 4 * (32 / best.BT) : 4;
-  best.CAP = (mode == 1 ? N : N * std::min(ly->L, 2 * kTapsMax)) + best.NKEY * best.PADM;
+  // room for the padding of either backward kernel (the specialised hybrid one pads to 8)
+  best.CAP = (mode == 1 ? N : N * std::min(ly->L, 2 * kTapsMax)) + best.NKEY * std::max(best.PADM, 8);
   return best;
+}
+
+// Specialised hybrid reverse scan (backward_hybrid.cuh): 32 sources per block, batch
+// tiles of 32, resident bucket lists.  Usable when N <= 512, K <= 8, MM <= 1 and the
+// lists fit in shared memory.
+struct HybPlan {
+  bool ok;
+  int CS, NT, CAPS, KMAX;
+  size_t smem;
+};
+static HybPlan plan_hybrid_fast(const delrec_layer* ly, const BwdPlan& bp) {
+  HybPlan h{};
+  h.ok = false;
+  if (ly->kind != DELREC_HYBRID || bp.MM > ly->K || ly->K > 8) return h;
+  h.NT = 32;
+  h.CS = cdiv(ly->N, h.NT);
+  if (h.CS > 16) return h;
+  h.CAPS = ((ly->N + 7 * (ly->K + 1)) + 7) / 8 * 8;   // buckets padded to 8 entries
+  h.KMAX = ly->K <= 4 ? 5 : 9;
+  h.smem = hyb_smem_plan(ly->N, h.NT, h.CAPS, ly->K, bp.TAPS, h.KMAX).total;
+  h.ok = h.smem <= kSmemLimit;
+  return h;
+}
+
+template <int KMAX>
+static int launch_hyb_t(const HybArgs& a, const HybPlan& h, cudaStream_t st) {
+  auto kern = k_bwd_hybrid<KMAX>;
+  int rc = set_smem(kern, h.smem);
+  if (rc) return rc;
+  if (h.CS > 8) DR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(h.CS * cdiv(a.B, 32));
+  cfg.blockDim = dim3(512);
+  cfg.dynamicSmemBytes = h.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = h.CS;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  DR_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
+  ++g_launches;
+  return DELREC_OK;
 }
 
 template <int MODE, int BT, int PPT>
@@ -450,15 +497,17 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
   }
   int2* ent = nullptr;
   int* boff = nullptr;
+  const HybPlan hp = plan_hybrid_fast(ly, bp);
   if (kind != DELREC_AXONAL) {
     ent = c.take<int2>((size_t)N * bp.CAP);
     boff = c.take<int>((size_t)N * (bp.NKEY + 1));
     const int nth = std::min(256, ((N + 31) / 32) * 32);
     const size_t sm = (size_t)nth * 8;
+    const int padm = hp.ok ? 8 : bp.PADM;
     if (kind == DELREC_HYBRID)
-      k_buckets<1><<<N, nth, sm, st>>>(N, bp.NKEY, bp.CAP, bp.PADM, W, offT, nullptr, s, ent, boff);
+      k_buckets<1><<<N, nth, sm, st>>>(N, bp.NKEY, bp.CAP, padm, W, offT, nullptr, s, ent, boff);
     else
-      k_buckets<2><<<N, nth, sm, st>>>(N, bp.NKEY, bp.CAP, bp.PADM, W, nullptr, dT, s, ent, boff);
+      k_buckets<2><<<N, nth, sm, st>>>(N, bp.NKEY, bp.CAP, padm, W, nullptr, dT, s, ent, boff);
     DR_LAUNCHED();
   }
   // ---- reverse scan
@@ -468,7 +517,15 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
   a.gy = gy; a.u = u; a.keep = ly->has_keep ? keep : nullptr; a.W = W;
   a.tap_l0 = tl0; a.tap_nt = tnt; a.tap_w = tw; a.ent = ent; a.boff = boff;
   a.dx = g->dx; a.gr = gr; a.gz = gz; a.w_smem = bp.w_smem; a.lif = make_lif(*lif);
-  if (bp.mode == 0) rc = launch_bwd_mode<0>(a, bp, st);
+  if (hp.ok) {
+    HybArgs h{};
+    h.T = T; h.B = B; h.N = N; h.K = ly->K; h.CS = hp.CS; h.NT = hp.NT; h.TAPS = bp.TAPS; h.MM = bp.MM;
+    h.CAPS = hp.CAPS; h.gy = gy; h.u = u; h.keep = ly->has_keep ? keep : nullptr;
+    h.tap_l0 = tl0; h.tap_nt = tnt; h.tap_w = tw; h.ent = ent; h.boff = boff; h.CAP = bp.CAP;
+    h.dx = g->dx; h.gr = gr; h.gz = gz; h.lif = a.lif;
+    if (hp.KMAX == 5) rc = launch_hyb_t<5>(h, hp, st);
+    else rc = launch_hyb_t<9>(h, hp, st);
+  } else if (bp.mode == 0) rc = launch_bwd_mode<0>(a, bp, st);
   else if (bp.mode == 1) rc = launch_bwd_mode<1>(a, bp, st);
   else rc = launch_bwd_mode<2>(a, bp, st);
   if (rc) return rc;
