@@ -116,6 +116,21 @@ int delrec_axonal_backward(const delrec_layer* layer, const delrec_lif* lif,
                            const float* keep, const delrec_grads* grads,
                            void* workspace, size_t workspace_bytes, void* stream);
 
+/* Same as delrec_axonal_forward but allocation-free: no reference counterpart.  It is for
+ * callers that cannot call cudaMalloc while the layer runs (all device memory handed to
+ * their own allocator, no device-wide synchronisation allowed in the loop, or a plugin
+ * host that forbids allocation after start-up).  Its scratch is a fixed 8 MiB device
+ * array inside the library (N <= 1024 neurons; larger layers get DELREC_ERR_WORKSPACE),
+ * held by every GPU that loads the library until the process exits.  The first call on
+ * a device looks the array up (cudaGetSymbolAddress), so make that first call before any
+ * stream capture.  All calls share the array: calls that overlap on the GPU (other
+ * streams, other threads) race on it.  Every byte it reads is written earlier in the
+ * same call, so nothing carries over between calls. */
+int delrec_axonal_forward_noalloc(const delrec_layer* layer, const delrec_lif* lif,
+                                  const float* x, const float* W, const float* bias,
+                                  const float* d, const float* s, const float* keep,
+                                  float* y, float* u, void* stream);
+
 /* ---- synaptic layer ---------------------------------------------------------------- */
 /* d (N,N) per connection, s (N) per source. */
 size_t delrec_synaptic_forward_workspace(const delrec_layer* layer);

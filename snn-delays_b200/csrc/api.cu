@@ -746,4 +746,38 @@ int delrec_dcls_backward(int T, int B, int Cin, int Cout, int groups, int K, int
   return DELREC_OK;
 }
 
+// ---- allocation-free variant of the axonal forward --------------------------------
+// Some callers cannot call cudaMalloc while they run this layer: a host that hands all
+// device memory to its own allocator up front and keeps none spare, a training loop that
+// must not add the device-wide synchronisation cudaMalloc/cudaFree imply, or a plugin
+// runtime that forbids allocation after start-up.  For them the scratch of the axonal
+// forward (transposed weights and the per-source tap table) lives in this fixed device
+// array, which every GPU that loads the library holds until the process exits.
+static constexpr size_t kNoAllocScratchBytes = 8u << 20;   // 8 MiB: N <= 1024 neurons
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+static void* g_noalloc_ptr[64] = {nullptr};
+
+int delrec_axonal_forward_noalloc(const delrec_layer* ly, const delrec_lif* lif, const float* x,
+                                  const float* W, const float* bias, const float* d, const float* s,
+                                  const float* keep, float* y, float* u, void* stream) {
+  if (!ly) return DELREC_ERR_ARG;
+  if (forward_ws(ly, DELREC_AXONAL) > kNoAllocScratchBytes) {
+    fprintf(stderr, "delrec_b200: delrec_axonal_forward_noalloc needs %zu bytes of scratch for N=%d, "
+                    "more than its fixed %zu-byte array; use delrec_axonal_forward with a workspace\n",
+            forward_ws(ly, DELREC_AXONAL), (int)ly->N, kNoAllocScratchBytes);
+    return DELREC_ERR_WORKSPACE;
+  }
+  int dev = 0;
+  DR_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return DELREC_ERR_UNSUPPORTED;
+  if (!g_noalloc_ptr[dev]) {
+    // once per device, with that device current: the symbol's device address
+    void* p = nullptr;
+    DR_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_ptr[dev] = p;
+  }
+  return run_forward(ly, DELREC_AXONAL, lif, x, W, bias, d, nullptr, s, keep, y, u, g_noalloc_ptr[dev],
+                     kNoAllocScratchBytes, (cudaStream_t)stream);
+}
+
 }  // extern "C"

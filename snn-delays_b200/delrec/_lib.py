@@ -55,6 +55,7 @@ _SIGS = {
     "delrec_synaptic_backward_workspace": (_S, [_P]),
     "delrec_hybrid_backward_workspace": (_S, [_P]),
     "delrec_axonal_forward": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _S, _P]),
+    "delrec_axonal_forward_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "delrec_synaptic_forward": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _S, _P]),
     "delrec_hybrid_forward": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _S, _P]),
     "delrec_axonal_backward": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _S, _P]),
