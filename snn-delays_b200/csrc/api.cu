@@ -284,8 +284,8 @@ static BwdPlan plan_backward(const delrec_layer* ly, int kind) {
 // tiles of 32, resident bucket lists.  Usable when N <= 512, K <= 8, MM <= 1 and the
 // lists fit in shared memory.
 struct HybPlan {
-  bool ok;
-  int CS, NT, CAPS, KMAX;
+  bool ok, coop;
+  int CS, NT, CAPS, KMAX, tiles;
   size_t smem;
 };
 static HybPlan plan_hybrid_fast(const delrec_layer* ly, const BwdPlan& bp) {
@@ -294,7 +294,10 @@ static HybPlan plan_hybrid_fast(const delrec_layer* ly, const BwdPlan& bp) {
   if (ly->kind != DELREC_HYBRID || bp.MM > ly->K || ly->K > 8) return h;
   h.NT = 32;
   h.CS = cdiv(ly->N, h.NT);
-  if (h.CS > 16) return h;
+  h.tiles = cdiv(ly->B, 32);
+  // one wave: a cooperative launch when every block fits on its own SM, else clusters
+  h.coop = h.CS * h.tiles <= kSMs;
+  if (!h.coop && h.CS > 16) return h;
   h.CAPS = ((ly->N + 7 * (ly->K + 1)) + 7) / 8 * 8;   // buckets padded to 8 entries
   h.KMAX = ly->K <= 4 ? 5 : 9;
   h.smem = hyb_smem_plan(ly->N, h.NT, h.CAPS, ly->K, bp.TAPS, h.KMAX).total;
@@ -304,7 +307,23 @@ static HybPlan plan_hybrid_fast(const delrec_layer* ly, const BwdPlan& bp) {
 
 template <int KMAX>
 static int launch_hyb_t(const HybArgs& a, const HybPlan& h, cudaStream_t st) {
-  auto kern = k_bwd_hybrid<KMAX>;
+  if (h.coop) {
+    auto kern = k_bwd_hybrid<KMAX, true>;
+    int rc = set_smem(kern, h.smem);
+    if (rc) return rc;
+    int per_sm = 0;
+    DR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 512, h.smem));
+    if (per_sm >= 1 && h.CS * h.tiles <= per_sm * kSMs) {
+      DR_CUDA(cudaMemsetAsync(a.arrive, 0, sizeof(unsigned int) * h.tiles, st));
+      HybArgs ac = a;
+      void* args[] = {(void*)&ac};
+      DR_CUDA(cudaLaunchCooperativeKernel((const void*)kern, dim3(h.CS * h.tiles), dim3(512), args, h.smem, st));
+      ++g_launches;
+      return DELREC_OK;
+    }
+    if (h.CS > 16) return DELREC_ERR_UNSUPPORTED;
+  }
+  auto kern = k_bwd_hybrid<KMAX, false>;
   int rc = set_smem(kern, h.smem);
   if (rc) return rc;
   if (h.CS > 8) DR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
@@ -446,6 +465,10 @@ static size_t backward_ws(const delrec_layer* ly, int kind) {
     c.take<int2>(N * (size_t)bp.CAP);
     c.take<int>(N * (size_t)(bp.NKEY + 1));
   }
+  if (kind == DELREC_HYBRID) {
+    c.take<float>((size_t)2 * cdiv(ly->B, 32) * N * 32);   // gr exchange (cooperative mode)
+    c.take<unsigned int>((size_t)cdiv(ly->B, 32));         // arrival counters
+  }
   const int parts = kind == DELREC_SYNAPTIC ? 3 : 1;
   c.take<float>((size_t)pp.splits * N * N * parts);   // pair partials
   if (kind == DELREC_SYNAPTIC) c.take<float>(N * N);   // ds per pair, summed
@@ -517,8 +540,15 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
   a.gy = gy; a.u = u; a.keep = ly->has_keep ? keep : nullptr; a.W = W;
   a.tap_l0 = tl0; a.tap_nt = tnt; a.tap_w = tw; a.ent = ent; a.boff = boff;
   a.dx = g->dx; a.gr = gr; a.gz = gz; a.w_smem = bp.w_smem; a.lif = make_lif(*lif);
+  float* grx = nullptr;
+  unsigned int* arrive = nullptr;
+  if (kind == DELREC_HYBRID) {
+    grx = c.take<float>((size_t)2 * cdiv(B, 32) * N * 32);
+    arrive = c.take<unsigned int>((size_t)cdiv(B, 32));
+  }
   if (hp.ok) {
     HybArgs h{};
+    h.grx = grx; h.arrive = arrive; h.spin_limit = 1ll << 22;
     h.T = T; h.B = B; h.N = N; h.K = ly->K; h.CS = hp.CS; h.NT = hp.NT; h.TAPS = bp.TAPS; h.MM = bp.MM;
     h.CAPS = hp.CAPS; h.gy = gy; h.u = u; h.keep = ly->has_keep ? keep : nullptr;
     h.tap_l0 = tl0; h.tap_nt = tnt; h.tap_w = tw; h.ent = ent; h.boff = boff; h.CAP = bp.CAP;

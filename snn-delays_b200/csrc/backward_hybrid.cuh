@@ -42,6 +42,10 @@ struct HybArgs {
   float* gr;
   float* gz;              // gz_m at gz + m*T*B*N, m = 0..MM
   LifK lif;
+  // cooperative mode: gr exchange through L2 instead of distributed shared memory
+  float* grx;             // [2][tiles][N][32]
+  unsigned int* arrive;   // [tiles] arrival counters, zero at launch
+  long long spin_limit;   // polls before a barrier gives up (sets ST_TIMEOUT)
 };
 
 struct HybSmem {
@@ -59,12 +63,19 @@ __host__ __device__ inline HybSmem hyb_smem_plan(int N, int NT, int CAPS, int K,
   return p;
 }
 
-template <int KMAX>
+// COOP = false: the blocks of a batch tile form a thread-block cluster and share gr
+//   through distributed shared memory (at most 16 blocks per cluster; a GPC hosts one
+//   16-block cluster, so at most 7 such clusters are co-resident on a B200).
+// COOP = true: a cooperative launch (every block co-resident, or the launch fails); the
+//   blocks of a tile publish their gr slices to a double-buffered L2 buffer and meet at
+//   an arrival counter per tile.  The wait polls with an iteration limit; on expiry the
+//   block records ST_TIMEOUT and leaves (its peers then expire at their next wait).
+template <int KMAX, bool COOP>
 __global__ void __launch_bounds__(512, 1) k_bwd_hybrid(HybArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
-  cg::cluster_group cl = cg::this_cluster();
+  __shared__ int s_abort;
   constexpr int BT = 32, NTH = 512, SPW = 2, PPT = 2;
-  const int rank = (int)cl.block_rank();
+  const int rank = COOP ? (int)(blockIdx.x % a.CS) : (int)cg::this_cluster().block_rank();
   const int N = a.N, T = a.T, B = a.B, NT = a.NT, K = a.K, MM = a.MM, tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
   const int tile = blockIdx.x / a.CS;
@@ -120,8 +131,11 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid(HybArgs a) {
   float lam[PPT];
 #pragma unroll
   for (int k = 0; k < PPT; ++k) lam[k] = 0.f;
+  if (tid == 0) s_abort = 0;
   __syncthreads();
-  cl.sync();
+  if (!COOP) cg::this_cluster().sync();
+  const size_t xtile = (size_t)N * BT;
+  unsigned int arrivals = 0;
 
   for (int t = T - 1; t >= 0; --t) {
     // ===== A: LIF backward of own pairs (p = tid + NTH k -> b = p / NT, o = p % NT)
@@ -153,20 +167,51 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid(HybArgs a) {
       }
       if (bl < BT && ol < nts) grc[(size_t)(o0 + ol) * BT + bl] = grv;
     }
-    // ===== B: publish the own slice of gr(t) to every block of the cluster
+    // ===== B: publish the own slice of gr(t) to every block of the tile
     __syncthreads();
-    cl.sync();  // the peers finished reading their copies of step t+1
-    if (a.CS > 1 && nts > 0) {
+    if (!COOP) {
+      cg::cluster_group cl = cg::this_cluster();
+      cl.sync();  // the peers finished reading their copies of step t+1
+      if (a.CS > 1 && nts > 0) {
+        const int n4 = nts * BT / 4;
+        const float4* src = (const float4*)(grc + (size_t)o0 * BT);
+        for (int v = tid; v < n4 * (a.CS - 1); v += NTH) {
+          int r = v / n4;
+          r += (r >= rank);
+          float4* dst = (float4*)cl.map_shared_rank(grc + (size_t)o0 * BT, r);
+          dst[v % n4] = src[v % n4];
+        }
+      }
+      cl.sync();
+    } else if (a.CS > 1) {
+      float* xb = a.grx + ((size_t)(t & 1) * (gridDim.x / a.CS) + tile) * xtile;
       const int n4 = nts * BT / 4;
       const float4* src = (const float4*)(grc + (size_t)o0 * BT);
-      for (int v = tid; v < n4 * (a.CS - 1); v += NTH) {
-        int r = v / n4;
-        r += (r >= rank);
-        float4* dst = (float4*)cl.map_shared_rank(grc + (size_t)o0 * BT, r);
-        dst[v % n4] = src[v % n4];
+      float4* dst = (float4*)(xb + (size_t)o0 * BT);
+      for (int v = tid; v < n4; v += NTH) __stcg(dst + v, src[v]);
+      __syncthreads();
+      arrivals += a.CS;
+      if (tid == 0) {
+        __threadfence();
+        atomicAdd(a.arrive + tile, 1u);
+        long long polls = 0;
+        unsigned int seen;
+        do {
+          asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(seen) : "l"(a.arrive + tile) : "memory");
+          if (++polls > a.spin_limit) { flag_status(ST_TIMEOUT); s_abort = 1; break; }
+        } while (seen < arrivals);
       }
+      __syncthreads();
+      if (s_abort) return;
+      // gather the peers' slices (L2; the own slice is already local)
+      const int rows4 = N * BT / 4;
+      const float4* xs = (const float4*)xb;
+      float4* gd = (float4*)grc;
+      const int own0 = o0 * BT / 4, own1 = (o0 + nts) * BT / 4;
+      for (int v = tid; v < rows4; v += NTH)
+        if (v < own0 || v >= own1) gd[v] = __ldcg(xs + v);
+      __syncthreads();
     }
-    cl.sync();
     // ===== C: bucket sums of the warp's sources into their rings
     const float* grl = grc + lane;
     for (int s = 0; s < SPW; ++s) {
@@ -212,7 +257,7 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid(HybArgs a) {
     }
     __syncthreads();  // gz written this step is read by other threads in A of step t-1
   }
-  cl.sync();
+  if (!COOP) cg::this_cluster().sync();
 }
 
 }  // namespace delrec

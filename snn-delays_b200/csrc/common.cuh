@@ -18,7 +18,7 @@ namespace delrec {
 // ---------------------------------------------------------------------------------
 // the library is one translation unit (api.cu), which owns this definition
 __device__ int g_status = 0;
-enum : int { ST_LAG_RANGE = 1 << 0, ST_INDEX_RANGE = 1 << 1, ST_SHAPE = 1 << 2 };
+enum : int { ST_LAG_RANGE = 1 << 0, ST_INDEX_RANGE = 1 << 1, ST_SHAPE = 1 << 2, ST_TIMEOUT = 1 << 3 };
 __device__ __forceinline__ void flag_status(int bit) { atomicOr(&g_status, bit); }
 
 // ---------------------------------------------------------------------------------
