@@ -4,9 +4,11 @@
  * All pointers are device pointers, tensors are fp32, contiguous, time-major (T,B,N).
  * Weights follow the reference's convention W[i,o] (row = target neuron i, column =
  * source neuron o): rec[b,i] = sum_o W[i,o] * (delayed spike of o).
- * Every entry point launches on `stream` (a cudaStream_t; NULL = legacy default stream),
- * allocates nothing, and returns DELREC_OK or an error code.  Scratch memory is passed
- * in by the caller: query its size with the matching *_workspace function.
+ * Every entry point launches on `stream` (a cudaStream_t; NULL = legacy default stream)
+ * and returns DELREC_OK or an error code.  Scratch memory is passed in by the caller:
+ * query its size with the matching *_workspace function.  The axonal and hybrid
+ * backward run their weight-gradient GEMMs through cuBLAS (on a slice of that
+ * workspace); the cuBLAS handle is created on the first such call on each device.
  *
  * Reference interfaces replaced (paths are inside ZiyadBekrar/SNN-delays):
  *   delrec_build_mask             triton_kernels/delays.py:13-29, 48-63 (build_mask,

@@ -2,6 +2,7 @@
 // launch planning (block sizes, cluster shapes, shared-memory budgets) and the kernel
 // sequences of each layer forward / backward.  No allocation happens here: all
 // scratch comes from the caller's workspace.
+#include <cublas_v2.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -10,6 +11,7 @@
 
 #include "backward.cuh"
 #include "backward_hybrid.cuh"
+#include "dense.cuh"
 #include "forward.cuh"
 #include "grads.cuh"
 #include "misc.cuh"
@@ -292,6 +294,7 @@ static HybPlan plan_hybrid_fast(const delrec_layer* ly, const BwdPlan& bp) {
   HybPlan h{};
   h.ok = false;
   if (ly->kind != DELREC_HYBRID || bp.MM > ly->K || ly->K > 8) return h;
+  if (ly->N > 512) return h;   // 16-bit byte offsets of the gr rows (512 rows of 128 B)
   h.NT = 32;
   h.CS = cdiv(ly->N, h.NT);
   h.tiles = cdiv(ly->B, 32);
@@ -447,6 +450,88 @@ static SrcPlan plan_src(const delrec_layer* ly) {
   return p;
 }
 
+// ---- tensor-core dW (dense.cuh) -------------------------------------------------
+static constexpr size_t kCublasWs = 32u << 20;
+static cublasHandle_t g_cublas[64] = {nullptr};
+
+static int cublas_for_device(cublasHandle_t* out) {
+  int dev = 0;
+  DR_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return DELREC_ERR_UNSUPPORTED;
+  if (!g_cublas[dev]) {
+    if (cublasCreate(&g_cublas[dev]) != CUBLAS_STATUS_SUCCESS) return DELREC_ERR_CUDA;
+  }
+  *out = g_cublas[dev];
+  return DELREC_OK;
+}
+
+// bytes of the tensor-core dW path: bf16 splits of gr and of each z variant, K+1 P
+// matrices, the cuBLAS workspace
+static size_t dense_dw_ws(const delrec_layer* ly, int nz, int nk) {
+  const size_t TBN = (size_t)ly->T * ly->B * ly->N, nn = (size_t)ly->N * ly->N;
+  Carve c(nullptr, (size_t)-1);
+  c.take<__nv_bfloat16>(TBN * 2);
+  c.take<__nv_bfloat16>(TBN * 2 * nz);
+  if (nk > 1) c.take<float>(nn * nk);
+  c.take<unsigned char>(kCublasWs);
+  return c.off;
+}
+
+// dW (N,N) from gr (T,B,N) and the z variants z + v*TBN, v = min(k, nz-1) for offset k
+static int dense_dw(const delrec_layer* ly, const float* gr, const float* z, int nz, int nk,
+                    const uint8_t* offT, float* dW, Carve& c, cudaStream_t st) {
+  const int N = ly->N, T = ly->T, B = ly->B;
+  const size_t TBN = (size_t)T * B * N, nn = (size_t)N * N;
+  __nv_bfloat16* g16 = c.take<__nv_bfloat16>(TBN * 2);
+  __nv_bfloat16* z16 = c.take<__nv_bfloat16>(TBN * 2 * nz);
+  float* P = nk > 1 ? c.take<float>(nn * nk) : dW;
+  void* cws = c.take<unsigned char>(kCublasWs);
+  if (!c.ok) return DELREC_ERR_WORKSPACE;
+  k_split_bf16<<<grid_for(TBN, 256), 256, 0, st>>>(gr, TBN, g16, g16 + TBN);
+  DR_LAUNCHED();
+  for (int v = 0; v < nz; ++v) {
+    k_split_bf16<<<grid_for(TBN, 256), 256, 0, st>>>(z + (size_t)v * TBN, TBN, z16 + (size_t)v * 2 * TBN,
+                                                     z16 + (size_t)v * 2 * TBN + TBN);
+    DR_LAUNCHED();
+  }
+  cublasHandle_t h;
+  int rc = cublas_for_device(&h);
+  if (rc) return rc;
+  if (cublasSetStream(h, st) != CUBLAS_STATUS_SUCCESS) return DELREC_ERR_CUDA;
+  if (cublasSetWorkspace(h, cws, kCublasWs) != CUBLAS_STATUS_SUCCESS) return DELREC_ERR_CUDA;
+  const float one = 1.f, zero = 0.f;
+  for (int k = 0; k < nk; ++k) {
+    const int rows = (T - k) * B;
+    float* Pk = P + (size_t)k * nn;
+    if (rows <= 0) {
+      DR_CUDA(cudaMemsetAsync(Pk, 0, nn * sizeof(float), st));
+      continue;
+    }
+    const int v = k < nz - 1 ? k : nz - 1;
+    const __nv_bfloat16* Zh = z16 + (size_t)v * 2 * TBN;
+    const __nv_bfloat16* Zl = Zh + TBN;
+    const __nv_bfloat16* Gh = g16 + (size_t)k * B * N;
+    const __nv_bfloat16* Gl = g16 + TBN + (size_t)k * B * N;
+    // column-major view: C'(o,i) = sum_r Z'(o,r) G'(i,r)  ->  row-major dW[i][o]
+    const __nv_bfloat16* As[3] = {Zh, Zh, Zl};
+    const __nv_bfloat16* Bs[3] = {Gh, Gl, Gh};
+    for (int p = 0; p < 3; ++p) {
+      cublasStatus_t e = cublasGemmEx(h, CUBLAS_OP_N, CUBLAS_OP_T, N, N, rows, &one, As[p], CUDA_R_16BF, N,
+                                      Bs[p], CUDA_R_16BF, N, p == 0 ? &zero : &one, Pk, CUDA_R_32F, N,
+                                      CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+      if (e != CUBLAS_STATUS_SUCCESS) {
+        fprintf(stderr, "delrec_b200: cublasGemmEx failed (%d)\n", (int)e);
+        return DELREC_ERR_CUDA;
+      }
+    }
+  }
+  if (nk > 1) {
+    k_pick_by_offset<<<grid_for(nn, 256), 256, 0, st>>>(N, offT, P, dW);
+    DR_LAUNCHED();
+  }
+  return DELREC_OK;
+}
+
 static size_t backward_ws(const delrec_layer* ly, int kind) {
   const BwdPlan bp = plan_backward(ly, kind);
   const PairPlan pp = plan_pairs(ly, bp.mode, nullptr);
@@ -471,6 +556,10 @@ static size_t backward_ws(const delrec_layer* ly, int kind) {
   }
   const int parts = kind == DELREC_SYNAPTIC ? 3 : 1;
   c.take<float>((size_t)pp.splits * N * N * parts);   // pair partials
+  if (kind != DELREC_SYNAPTIC) {
+    const size_t dws = dense_dw_ws(ly, bp.MM + 1, kind == DELREC_HYBRID ? ly->K + 1 : 1);
+    c.take<unsigned char>(dws);
+  }
   if (kind == DELREC_SYNAPTIC) c.take<float>(N * N);   // ds per pair, summed
   c.take<float>((size_t)sp.splits * N * (bp.TAPS + 1)); // source partials
   return c.off;
@@ -570,7 +659,14 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
     k_axonal_z<<<grid_for(TBN, 256), 256, 0, st>>>(T, B, N, bp.TAPS, bp.MM + 1, y, tl0, tnt, tw, z);
     DR_LAUNCHED();
   }
-  if (g->dW || (kind == DELREC_SYNAPTIC && (g->dd || g->ds))) {
+  if (g->dW && kind != DELREC_SYNAPTIC) {
+    // tensor-core path: K+1 shifted GEMMs and a per-synapse pick
+    const size_t dws = dense_dw_ws(ly, bp.MM + 1, kind == DELREC_HYBRID ? ly->K + 1 : 1);
+    unsigned char* region = c.take<unsigned char>(dws);
+    Carve dc(region, dws);
+    rc = dense_dw(ly, gr, z, bp.MM + 1, kind == DELREC_HYBRID ? ly->K + 1 : 1, offT, g->dW, dc, st);
+    if (rc) return rc;
+  } else if (g->dW || (kind == DELREC_SYNAPTIC && (g->dd || g->ds))) {
     PairArgs pa{};
     pa.T = T; pa.B = B; pa.N = N; pa.KR = pp.KR; pa.BCH = pp.BCH; pa.rows_per_split = pp.rows_per_split;
     pa.gr = gr; pa.Y = kind == DELREC_SYNAPTIC ? y : z; pa.offT = offT; pa.dT = dT; pa.s = s; pa.W = W;

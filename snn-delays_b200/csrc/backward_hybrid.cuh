@@ -103,7 +103,7 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid(HybArgs a) {
       const int tot = a.boff[(size_t)(o0 + ol) * (K + 2) + K + 1];
       if (pos < tot) en = a.ent[(size_t)(o0 + ol) * a.CAP + pos];
     }
-    sidx[e] = (uint16_t)en.x;
+    sidx[e] = (uint16_t)(en.x * (BT * 4));   // byte offset of gr row i (N <= 512)
     sw[e] = __int_as_float(en.y);
   }
   for (int e = tid; e < NT * (K + 2); e += NTH) {
@@ -212,8 +212,9 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid(HybArgs a) {
         if (v < own0 || v >= own1) gd[v] = __ldcg(xs + v);
       __syncthreads();
     }
-    // ===== C: bucket sums of the warp's sources into their rings
-    const float* grl = grc + lane;
+    // ===== C: bucket sums of the warp's sources into their rings.  The gather uses
+    // 32-bit shared-memory addresses: lane base + the entry's precomputed row offset.
+    const uint32_t gbase = (uint32_t)__cvta_generic_to_shared(grc) + lane * 4;
     for (int s = 0; s < SPW; ++s) {
       const int ol = warp * SPW + s;
       if (ol >= nts) continue;
@@ -226,19 +227,28 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid(HybArgs a) {
         float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
         // buckets start and end on multiples of 8 entries (16-byte aligned index loads)
         if (((beg | end) & 7) != 0) { flag_status(ST_INDEX_RANGE); continue; }
-        int e = beg;
-        for (; e + 8 <= end; e += 8) {
-          const uint4 i8 = *(const uint4*)(ix + e);               // 8 x u16
+#pragma unroll 2
+        for (int e = beg; e < end; e += 8) {
+          const uint4 i8 = *(const uint4*)(ix + e);               // 8 x u16 byte offsets
           const float4 wa = *(const float4*)(wv + e);
           const float4 wb = *(const float4*)(wv + e + 4);
-          acc0 = fmaf(wa.x, grl[(i8.x & 0xffffu) * BT], acc0);
-          acc1 = fmaf(wa.y, grl[(i8.x >> 16) * BT], acc1);
-          acc2 = fmaf(wa.z, grl[(i8.y & 0xffffu) * BT], acc2);
-          acc3 = fmaf(wa.w, grl[(i8.y >> 16) * BT], acc3);
-          acc0 = fmaf(wb.x, grl[(i8.z & 0xffffu) * BT], acc0);
-          acc1 = fmaf(wb.y, grl[(i8.z >> 16) * BT], acc1);
-          acc2 = fmaf(wb.z, grl[(i8.w & 0xffffu) * BT], acc2);
-          acc3 = fmaf(wb.w, grl[(i8.w >> 16) * BT], acc3);
+          float g0, g1, g2, g3, g4, g5, g6, g7;
+          asm volatile("ld.shared.f32 %0, [%1];" : "=f"(g0) : "r"(gbase + (i8.x & 0xffffu)));
+          asm volatile("ld.shared.f32 %0, [%1];" : "=f"(g1) : "r"(gbase + (i8.x >> 16)));
+          asm volatile("ld.shared.f32 %0, [%1];" : "=f"(g2) : "r"(gbase + (i8.y & 0xffffu)));
+          asm volatile("ld.shared.f32 %0, [%1];" : "=f"(g3) : "r"(gbase + (i8.y >> 16)));
+          asm volatile("ld.shared.f32 %0, [%1];" : "=f"(g4) : "r"(gbase + (i8.z & 0xffffu)));
+          asm volatile("ld.shared.f32 %0, [%1];" : "=f"(g5) : "r"(gbase + (i8.z >> 16)));
+          asm volatile("ld.shared.f32 %0, [%1];" : "=f"(g6) : "r"(gbase + (i8.w & 0xffffu)));
+          asm volatile("ld.shared.f32 %0, [%1];" : "=f"(g7) : "r"(gbase + (i8.w >> 16)));
+          acc0 = fmaf(wa.x, g0, acc0);
+          acc1 = fmaf(wa.y, g1, acc1);
+          acc2 = fmaf(wa.z, g2, acc2);
+          acc3 = fmaf(wa.w, g3, acc3);
+          acc0 = fmaf(wb.x, g4, acc0);
+          acc1 = fmaf(wb.y, g5, acc1);
+          acc2 = fmaf(wb.z, g6, acc2);
+          acc3 = fmaf(wb.w, g7, acc3);
         }
         if (t - k >= 0) {
           float* cell = rg + ((t - k) % KMAX) * 32;
