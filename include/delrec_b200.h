@@ -200,6 +200,11 @@ int delrec_clear_status(void);
 const char* delrec_version(void);
 /* Number of kernels this library has launched in this process (host-side counter). */
 unsigned long long delrec_launch_count(void);
+/* Measurement hooks: while enabled, every reverse-scan launch (the backward's time loop)
+ * is bracketed by CUDA events on its stream; delrec_scan_time synchronizes on them and
+ * returns the summed milliseconds and the number of launches since enabling. */
+int delrec_scan_timing(int enable);
+int delrec_scan_time(double* total_ms, int* launches);
 
 #ifdef __cplusplus
 }

@@ -39,6 +39,19 @@ static inline int pow2_at_least(int x) {
   } while (0)
 static unsigned long long g_launches = 0;  // kernels issued by this library (host counter)
 
+// Optional timing of the reverse-scan kernels: CUDA events recorded on the launching
+// stream around each scan launch while enabled (delrec_scan_timing).
+static bool g_scan_timing = false;
+static cudaEvent_t g_ev[512][2];
+static int g_ev_n = 0;
+static void scan_mark(int which, cudaStream_t st) {
+  if (!g_scan_timing || g_ev_n >= 512) return;
+  cudaEvent_t& e = g_ev[g_ev_n][which];
+  if (!e) cudaEventCreate(&e);
+  cudaEventRecord(e, st);
+  if (which == 1) ++g_ev_n;
+}
+
 #define DR_LAUNCHED()                                                      \
   do {                                                                     \
     ++g_launches;                                                          \
@@ -320,7 +333,9 @@ static int launch_hyb_t(const HybArgs& a, const HybPlan& h, cudaStream_t st) {
       DR_CUDA(cudaMemsetAsync(a.arrive, 0, sizeof(unsigned int) * h.tiles, st));
       HybArgs ac = a;
       void* args[] = {(void*)&ac};
+      scan_mark(0, st);
       DR_CUDA(cudaLaunchCooperativeKernel((const void*)kern, dim3(h.CS * h.tiles), dim3(512), args, h.smem, st));
+      scan_mark(1, st);
       ++g_launches;
       return DELREC_OK;
     }
@@ -342,7 +357,9 @@ static int launch_hyb_t(const HybArgs& a, const HybPlan& h, cudaStream_t st) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  scan_mark(0, st);
   DR_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
+  scan_mark(1, st);
   ++g_launches;
   return DELREC_OK;
 }
@@ -365,7 +382,9 @@ static int launch_bwd_t(const BwdArgs& a, const BwdPlan& p, cudaStream_t st) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  scan_mark(0, st);
   DR_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
+  scan_mark(1, st);
   ++g_launches;
   return DELREC_OK;
 }
@@ -726,6 +745,27 @@ extern "C" {
 const char* delrec_version(void) { return "delrec_b200 0.1 (sm_100a)"; }
 
 unsigned long long delrec_launch_count(void) { return g_launches; }
+
+int delrec_scan_timing(int enable) {
+  g_scan_timing = enable != 0;
+  g_ev_n = 0;
+  return DELREC_OK;
+}
+
+int delrec_scan_time(double* total_ms, int* launches) {
+  if (!total_ms || !launches) return DELREC_ERR_ARG;
+  double sum = 0.0;
+  for (int i = 0; i < g_ev_n; ++i) {
+    DR_CUDA(cudaEventSynchronize(g_ev[i][1]));
+    float ms = 0.f;
+    DR_CUDA(cudaEventElapsedTime(&ms, g_ev[i][0], g_ev[i][1]));
+    sum += ms;
+  }
+  *total_ms = sum;
+  *launches = g_ev_n;
+  g_ev_n = 0;
+  return DELREC_OK;
+}
 
 int delrec_get_status(int* out) {
   if (!out) return DELREC_ERR_ARG;

@@ -72,6 +72,8 @@ _SIGS = {
     "delrec_clear_status": (_I, []),
     "delrec_version": (ctypes.c_char_p, []),
     "delrec_launch_count": (ctypes.c_ulonglong, []),
+    "delrec_scan_timing": (_I, [_I]),
+    "delrec_scan_time": (_I, [_P, _P]),
 }
 
 _lib = None
@@ -151,6 +153,18 @@ def lif_struct(tau, v_threshold, v_reset, detach_reset, surrogate_id, gamma, alp
 
 def launch_count() -> int:
     return int(lib().delrec_launch_count())
+
+
+def scan_timing(enable: bool):
+    check(lib().delrec_scan_timing(int(enable)), "delrec_scan_timing")
+
+
+def scan_time():
+    """(total milliseconds, launches) of the reverse-scan kernels timed since enabling."""
+    ms = ctypes.c_double(0.0)
+    n = ctypes.c_int(0)
+    check(lib().delrec_scan_time(ctypes.byref(ms), ctypes.byref(n)), "delrec_scan_time")
+    return ms.value, n.value
 
 
 def status() -> int:
