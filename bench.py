@@ -93,46 +93,77 @@ def loss_fn(out, labels):
 # clocks sampled during the timed region
 # ----------------------------------------------------------------------------------
 class ClockSampler:
-    def __init__(self, index):
-        self.index = index
-        self.samples = []
-        self._stop = threading.Event()
-        self._t = None
-
-    def _run(self):
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+    """``nvidia-smi -lms 100`` running for the life of the ``with`` block; the summary
+    keeps the samples stamped inside [begin(), end()] (the timed region), or the one
+    nearest to it when the region is shorter than the sampling period."""
+    QUERY = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
              "clocks_event_reasons.sw_power_cap")
-        while not self._stop.is_set():
-            try:
-                out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
-                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
-                                     timeout=5).stdout.strip()
-                if out:
-                    self.samples.append([v.strip() for v in out.split(",")])
-            except Exception:
-                pass
-            self._stop.wait(0.2)
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+    def __init__(self, index):
+        self.index = index
+        self.samples = []          # (wall time, [fields])
+        self._proc = None
+        self._t = None
+        self._t0 = self._t1 = None
+
+    def _read(self):
+        for line in self._proc.stdout:
+            f = [v.strip() for v in line.strip().split(",")]
+            if len(f) >= 7:
+                self.samples.append((time.time(), f))
 
     def __enter__(self):
-        self._t = threading.Thread(target=self._run, daemon=True)
-        self._t.start()
+        try:
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+            t_wait = time.time() + 5.0
+            while not self.samples and time.time() < t_wait:   # sampler is live
+                time.sleep(0.02)
+        except OSError:
+            self._proc = None
         return self
 
+    def begin(self):
+        self._t0 = time.time()
+
+    def end(self):
+        self._t1 = time.time()
+
     def __exit__(self, *a):
-        self._stop.set()
-        self._t.join(timeout=10)
+        if self._proc is not None:
+            time.sleep(0.15)
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+            self._t.join(timeout=5)
 
     def summary(self):
         if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
-        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for s in self.samples for i in range(4)
-                          if len(s) > 4 + i and s[4 + i].lower() == "active"})
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        t0 = self._t0 if self._t0 is not None else self.samples[0][0]
+        t1 = self._t1 if self._t1 is not None else self.samples[-1][0]
+        inside = [f for (ts, f) in self.samples if t0 <= ts <= t1]
+        if not inside:
+            inside = [min(self.samples, key=lambda s: abs(s[0] - 0.5 * (t0 + t1)))[1]]
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+        sm = [x for x in (num(f[0]) for f in inside) if x is not None]
+        mx = [x for x in (num(f[1]) for f in inside) if x is not None]
+        reasons = sorted({self.NAMES[i] for f in inside for i in range(4) if f[3 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.samples)}
+                "reasons": reasons, "samples": len(inside)}
 
 
 # ----------------------------------------------------------------------------------
@@ -152,18 +183,9 @@ def dist_setup(n_gpus):
 
 
 def allreduce_grads(params, ws):
-    if ws == 1:
-        return
-    import torch.distributed as dist
-    grads = [p.grad for p in params if p.grad is not None]
-    flat = torch.cat([g.reshape(-1) for g in grads])
-    dist.all_reduce(flat)
-    flat.div_(ws)
-    off = 0
-    for g in grads:
-        n = g.numel()
-        g.copy_(flat[off:off + n].view_as(g))
-        off += n
+    if ws > 1:
+        from delrec.data_parallel import allreduce_gradients
+        allreduce_gradients(params)
 
 
 def barrier(ws):
@@ -230,19 +252,31 @@ def cpu_step_fn(model, spec, cfg):
     return step
 
 
-def time_cpu(model, spec, cfg, sample_b, steps, threads):
-    torch.set_num_threads(threads)
-    step = cpu_step_fn(model, spec, cfg)
-    x, labels = make_inputs(spec, sample_b, seed=2)
-    step(x, labels)  # warm
+def _cpu_timed_steps(step, x, labels, warmup, steps, budget_s):
+    """Median seconds per oracle step.  Warm-up steps run on the first tenth of the
+    timesteps (they only warm the allocator and thread pool); timed steps run the full
+    sample and stop early once ``budget_s`` is spent (at least one step always runs)."""
+    T = x.shape[0]
+    xw = x[: max(1, T // 10)].contiguous()
+    for _ in range(warmup):
+        step(xw, labels)
     times = []
+    t_start = time.perf_counter()
     for _ in range(steps):
         t0 = time.perf_counter()
         step(x, labels)
         times.append(time.perf_counter() - t0)
-    med = statistics.median(times)
-    units = sample_b * spec["T"]
-    return units / med, med
+        if time.perf_counter() - t_start > budget_s:
+            break
+    return statistics.median(times), len(times)
+
+
+def time_cpu(model, spec, cfg, sample_b, steps, threads, warmup=1, budget_s=40.0):
+    torch.set_num_threads(threads)
+    step = cpu_step_fn(model, spec, cfg)
+    x, labels = make_inputs(spec, sample_b, seed=2)
+    med, done = _cpu_timed_steps(step, x, labels, warmup, steps, budget_s)
+    return sample_b * spec["T"] / med, med, done
 
 
 def run_reference_arm(args, spec):
@@ -250,24 +284,18 @@ def run_reference_arm(args, spec):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
     model, cfg = build_model(spec, args.cpu_sample_b, "cpu")
     x, labels = make_inputs(spec, args.cpu_sample_b, seed=2)
     step = cpu_step_fn(model, spec, cfg)
-    torch.set_num_threads(threads)
-    for _ in range(args.warmup):
-        step(x, labels)
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        step(x, labels)
-        times.append(time.perf_counter() - t0)
-    med = statistics.median(times)
+    med, done = _cpu_timed_steps(step, x, labels, args.warmup, args.steps, args.cpu_budget)
     value = args.cpu_sample_b * spec["T"] / med
-    sample = (f"{args.cpu_sample_b} samples x T={spec['T']} of {args.config} per step "
-              f"(the full per-GPU batch is {spec['B']})")
+    sample = (f"{args.cpu_sample_b} sample(s) x T={spec['T']} of {args.config} per step, median of "
+              f"{done} step(s) ({med:.1f} s/step; the full per-GPU batch is {spec['B']})")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": med * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "steps": args.steps, "steps_timed": done, "warmup": args.warmup, "ms_per_step": med * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
             "config": {"workload": args.config, "model": spec["model"], "hidden": spec["hidden"],
                        "T": spec["T"], "batch_per_step": args.cpu_sample_b},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
@@ -288,12 +316,14 @@ def firing_rates(model):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="cfg4_ssc_hybrid_2x512", choices=list(CONFIGS))
-    ap.add_argument("--cpu-sample-b", type=int, default=2)
-    ap.add_argument("--cpu-steps", type=int, default=3)
+    ap.add_argument("--cpu-sample-b", type=int, default=64)
+    ap.add_argument("--cpu-steps", type=int, default=1)
+    ap.add_argument("--cpu-budget", type=float, default=150.0,
+                    help="seconds of timed CPU steps after which the reference arm stops early")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--T", type=int, default=None, help="override T (profiling of small cases)")
@@ -343,11 +373,13 @@ def main():
     barrier(ws)
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
+        clk.begin()
         start.record()
         for _ in range(args.steps):
             step(x, labels)
         end.record()
         torch.cuda.synchronize()
+        clk.end()
     barrier(ws)
     launches = _lib.launch_count() - launches0
     ms = max_over_ranks(start.elapsed_time(end), ws) / args.steps
@@ -376,17 +408,20 @@ def main():
         e2e = {"value": units / (ms2 / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": int(xh.numel() * 4 + lh.numel() * 8), "d2h_bytes_per_step": 4}
 
-    # ---- dominant kernel roofline: the reverse scan of one hybrid layer, timed alone
-    roof = roofline_probe(model, x, labels, dev) if rank == 0 else None
+    # ---- dominant kernel roofline: the reverse-scan launches of two more training
+    #      steps, each bracketed by CUDA events on its own stream inside the library
+    #      (every rank runs the steps: they contain the gradient all-reduce)
+    roof = roofline_probe(model, step, x, labels, spec, B)
+    step_roof = step_roofline(spec, B, ms)
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
         threads = os.cpu_count() or 1
         model_cpu, cfg_cpu = build_model(spec, args.cpu_sample_b, "cpu")
-        v, med = time_cpu(model_cpu, spec, cfg_cpu, args.cpu_sample_b, args.cpu_steps, threads)
+        v, med, done = time_cpu(model_cpu, spec, cfg_cpu, args.cpu_sample_b, args.cpu_steps, threads)
         cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"{args.cpu_sample_b} samples x T={spec['T']} of the same model per step, "
-                         f"median of {args.cpu_steps} ({med:.1f} s/step)"}
+               "sample": f"{args.cpu_sample_b} sample(s) x T={spec['T']} of the same model per step "
+                         f"(oracle fwd + autograd BPTT), median of {done} ({med:.1f} s/step)"}
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
@@ -398,53 +433,111 @@ def main():
                            "l2": "inputs larger than L2 (x is T*B*C*4 bytes per step)",
                            "firing_rates": rates},
                 "gpu_launches": launches, "clocks": clk.summary(), "e2e": e2e,
-                "roofline": roof, "cpu_baseline": cpu}
+                "roofline": roof, "step_roofline": step_roof, "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)
     if ws > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
 
 
-def roofline_probe(model, x, labels, dev):
-    """Times the hybrid layer's reverse scan (the dominant kernel) on its own with CUDA
-    events on the launching stream, and converts its algorithmic flops to TFLOP/s.
-    Algorithmic work per launch: the recurrent contraction of the backward,
-    2*N^2 flops per sample-timestep (gz = W^T gr with the per-synapse shift)."""
-    from delrec import functional as Fn
-    from delrec import networks
-    peaks = {}
+def _peaks():
     try:
-        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
     except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def _profiled_traffic(kernel):
+    """DRAM bytes per sample-timestep of ``kernel`` from the committed ncu summary
+    (profiles/<kernel>.txt, line ``dram_bytes_per_sample_step: <x>``), or None."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}.txt")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_sample_step:"):
+                    return float(line.split(":", 1)[1])
+    except OSError:
         pass
+    return None
+
+
+def roofline_probe(model, step, x, labels, spec, B):
+    """Average duration of the reverse-scan kernel (the dominant kernel of the step) over
+    the launches of two training steps, timed with CUDA events recorded on the stream
+    each launch is issued on, and its algorithmic throughput: the recurrent contraction
+    gz = W^T gr of the backward scan, 2*N^2 flops per sample-timestep, 2*N^2*B*T per
+    launch.  Peak: the measured sustained bf16 tensor rate (the kernel runs inside a
+    seconds-long training step)."""
+    from delrec import _lib
     rec = [m for m in model.layers if hasattr(m, "recurrent_weights")]
     if not rec:
         return None
-    layer = rec[0]
-    T, B = x.shape[0], x.shape[1]
-    N = layer.neurons
-    with torch.no_grad():
-        h = model.layers[0](x)
-    h = h.detach().requires_grad_(True)
-    y = layer(h)
-    gy = torch.randn_like(y)
-    torch.cuda.synchronize()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 3
-    s.record()
-    for _ in range(reps):
-        torch.autograd.grad(y, [h], gy, retain_graph=True)
-    e.record()
-    torch.cuda.synchronize()
-    ms = s.elapsed_time(e) / reps
+    _lib.scan_timing(True)
+    try:
+        for _ in range(2):
+            step(x, labels)
+        torch.cuda.synchronize()
+        total_ms, n = _lib.scan_time()
+    finally:
+        _lib.scan_timing(False)
+    if n == 0:
+        return None
+    N = rec[0].neurons
+    T = spec["T"]
+    ms = total_ms / n
     flops = 2.0 * N * N * B * T
-    peak = peaks.get("bf16_tflops")
+    peaks, src = _peaks()
+    peak = peaks["bf16_tflops_sustained"]
     achieved = flops / (ms / 1e3) / 1e12
-    return {"bound": "tensor", "kernel": "layer backward (reverse scan + gradient reductions)",
-            "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-            "frac": (achieved / peak) if peak else None, "traffic": None,
-            "ms_per_launch": ms, "flops_per_launch": flops,
-            "peak_source": "MEASURED_PEAKS.json bf16_tflops (measured)" if peak else "absent"}
+    per_unit = _profiled_traffic("k_bwd_hybrid") if spec["model"].endswith("hybrid_delays") else None
+    return {"bound": "tensor", "kernel": "k_bwd_hybrid (reverse scan of one recurrent layer)",
+            "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "traffic": per_unit * B * T if per_unit else None,
+            "ms_per_launch": ms, "launches_timed": n, "flops_per_launch": flops,
+            "peak_source": f"bf16_tflops_sustained ({src})",
+            "traffic_source": "ncu dram bytes per sample-timestep of a T=50 capture, scaled to B*T"
+                              if per_unit else None}
+
+
+def step_algorithmic(spec, B):
+    """Algorithmic flops and compulsory HBM bytes of one training step (per GPU).
+    Flops: every contraction counted dense (2 flops per multiply-add) -- the input
+    projection forward and weight gradient, for each recurrent layer the forward
+    contraction, the backward contraction and the weight gradient, the hidden-to-hidden
+    projection forward, input gradient and weight gradient, and the readout likewise.
+    Bytes: the input spikes read once, and per hidden layer the projected current, the
+    membrane and spike records written by the forward and read by the backward, and
+    the current gradient written and read (fp32)."""
+    T, C, K = spec["T"], spec["C"], spec["K"]
+    hid = spec["hidden"]
+    TB = T * B
+    flops = 2 * 2.0 * C * hid[0] * TB
+    prev = None
+    for N in hid:
+        if prev is not None:
+            flops += 3 * 2.0 * prev * N * TB
+        flops += 3 * 2.0 * N * N * TB
+        prev = N
+    flops += 3 * 2.0 * hid[-1] * K * TB
+    nbytes = 4.0 * TB * C
+    for N in hid:
+        nbytes += 4.0 * TB * N * (2 + 2 * 2 + 2)
+    return flops, nbytes
+
+
+def step_roofline(spec, B, ms):
+    """The step's floor time: the slower of its algorithmic flops at the measured
+    sustained bf16 tensor rate and its compulsory bytes at the measured HBM bandwidth;
+    frac = floor / measured step time."""
+    flops, nbytes = step_algorithmic(spec, B)
+    peaks, src = _peaks()
+    t_flops = flops / (peaks["bf16_tflops_sustained"] * 1e12)
+    t_bytes = nbytes / (peaks["hbm_gbs"] * 1e9)
+    floor_ms = max(t_flops, t_bytes) * 1e3
+    return {"flops": flops, "bytes": nbytes, "floor_ms": floor_ms,
+            "bound": "tensor" if t_flops >= t_bytes else "hbm", "frac": floor_ms / ms,
+            "peak_source": src}
 
 
 if __name__ == "__main__":
