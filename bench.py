@@ -501,43 +501,46 @@ def roofline_probe(model, step, x, labels, spec, B):
 
 
 def step_algorithmic(spec, B):
-    """Algorithmic flops and compulsory HBM bytes of one training step (per GPU).
-    Flops: every contraction counted dense (2 flops per multiply-add) -- the input
-    projection forward and weight gradient, for each recurrent layer the forward
-    contraction, the backward contraction and the weight gradient, the hidden-to-hidden
-    projection forward, input gradient and weight gradient, and the readout likewise.
-    Bytes: the input spikes read once, and per hidden layer the projected current, the
-    membrane and spike records written by the forward and read by the backward, and
-    the current gradient written and read (fp32)."""
+    """Algorithmic flops and HBM bytes of one training step (per GPU), per unit (one
+    sample x one timestep) times B*T.
+    Flops (dense-equivalent, 2 per multiply-add): each recurrent delay layer 6*N^2 (forward
+    contraction, backward contraction gz = W^T gr, weight gradient); each Linear in->out
+    6*in*out (forward, input gradient, weight gradient), 4*in*out for the first one (its
+    input needs no gradient).
+    Bytes (fp32 tensors at op boundaries): each delay layer 28*N (forward reads x, writes
+    y and the saved state; backward reads gy, the state and the spikes, writes dx); each
+    Linear 4*(in+out) forward plus 4*(2*out+in) backward, 4*(out+in) for the first."""
     T, C, K = spec["T"], spec["C"], spec["K"]
     hid = spec["hidden"]
-    TB = T * B
-    flops = 2 * 2.0 * C * hid[0] * TB
-    prev = None
-    for N in hid:
-        if prev is not None:
-            flops += 3 * 2.0 * prev * N * TB
-        flops += 3 * 2.0 * N * N * TB
-        prev = N
-    flops += 3 * 2.0 * hid[-1] * K * TB
-    nbytes = 4.0 * TB * C
-    for N in hid:
-        nbytes += 4.0 * TB * N * (2 + 2 * 2 + 2)
-    return flops, nbytes
+    flops = 0.0
+    nbytes = 0.0
+    dims = [C] + list(hid)
+    for j, N in enumerate(hid):
+        fin = dims[j]
+        first = j == 0
+        flops += (4.0 if first else 6.0) * fin * N + 6.0 * N * N
+        nbytes += 4.0 * (fin + N) + (4.0 * (N + fin) if first else 4.0 * (2 * N + fin)) + 28.0 * N
+    flops += 6.0 * hid[-1] * K
+    nbytes += 4.0 * (hid[-1] + K) + 4.0 * (2 * K + hid[-1])
+    units = T * B
+    return flops * units, nbytes * units
 
 
 def step_roofline(spec, B, ms):
-    """The step's floor time: the slower of its algorithmic flops at the measured
-    sustained bf16 tensor rate and its compulsory bytes at the measured HBM bandwidth;
-    frac = floor / measured step time."""
+    """The step's floor time: the slower of its algorithmic flops at the fp32-accurate
+    tensor rate (the measured sustained bf16 rate / 3: a 3-product bf16 split carries an
+    fp32 contraction) and its algorithmic bytes at the measured HBM bandwidth; frac =
+    floor / measured step time."""
     flops, nbytes = step_algorithmic(spec, B)
     peaks, src = _peaks()
-    t_flops = flops / (peaks["bf16_tflops_sustained"] * 1e12)
+    p_fp32acc = peaks["bf16_tflops_sustained"] / 3.0
+    t_flops = flops / (p_fp32acc * 1e12)
     t_bytes = nbytes / (peaks["hbm_gbs"] * 1e9)
     floor_ms = max(t_flops, t_bytes) * 1e3
     return {"flops": flops, "bytes": nbytes, "floor_ms": floor_ms,
             "bound": "tensor" if t_flops >= t_bytes else "hbm", "frac": floor_ms / ms,
-            "peak_source": src}
+            "peak_tflops_fp32acc": p_fp32acc, "peak_hbm_gbs": peaks["hbm_gbs"],
+            "peak_source": f"bf16_tflops_sustained/3 and hbm_gbs ({src})"}
 
 
 if __name__ == "__main__":
