@@ -32,6 +32,8 @@
  *                                 the model zoo (networks.py:84-96), no recurrence
  *   delrec_dcls_forward/backward  networks.py:43-50 (dcls_module.forward: DCLS 0.1.1 Gaussian
  *                                 kernel construction + causal conv1d over time)
+ *   delrec_linear_forward/backward  the torch.nn.Linear projections between the delay layers
+ *                                 and the readout (networks.py:84-96, 140-181)
  */
 #ifndef DELREC_B200_H
 #define DELREC_B200_H
@@ -191,6 +193,24 @@ int delrec_dcls_backward(int T, int B, int Cin, int Cout, int groups, int K, int
                          const float* SIG, const float* gout, float* dx, float* dweight,
                          float* dP, float* dSIG, float* dbias,
                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- feedforward projection ------------------------------------------------------- */
+/* out (M,N) = x (M,K) . W^T + bias, W (N,K) as torch.nn.Linear, bias (N) or NULL.
+ * Runs on bf16 tensor cores with fp32 accuracy: each fp32 operand is split exactly into
+ * three bf16 pieces and the piece products with i + j <= 2 are summed with fp32
+ * accumulation.  x_binary = 1 promises x in {0, 1} (spike trains: three products instead
+ * of six); a violated promise sets the status word.  The GEMMs run through cuBLAS on a
+ * slice of the workspace. */
+size_t delrec_linear_forward_workspace(int M, int K, int N, int x_binary);
+int delrec_linear_forward(int M, int K, int N, const float* x, const float* W, const float* bias,
+                          int x_binary, float* out, void* workspace, size_t workspace_bytes,
+                          void* stream);
+/* gout (M,N); dx (M,K), dW (N,K), dbias (N): any may be NULL (x may be NULL when dW and
+ * dbias are, W when dx is). */
+size_t delrec_linear_backward_workspace(int M, int K, int N, int x_binary);
+int delrec_linear_backward(int M, int K, int N, const float* x, const float* W, const float* gout,
+                           int x_binary, float* dx, float* dW, float* dbias, void* workspace,
+                           size_t workspace_bytes, void* stream);
 
 /* ---- device status word ------------------------------------------------------------ */
 /* Kernels record internal inconsistencies (an out-of-range lag or index that was

@@ -14,6 +14,7 @@
 #include "dense.cuh"
 #include "forward.cuh"
 #include "grads.cuh"
+#include "linear.cuh"
 #include "misc.cuh"
 #include "prep.cuh"
 
@@ -458,14 +459,10 @@ static int launch_pairs(int mode, const PairArgs& a, const PairPlan& p, int N, c
   return launch_pairs_b<2, 16>(a, p, N, st);
 }
 
-struct SrcPlan { int splits, rows_per_split; };
+struct SrcPlan { int splits; };
 static SrcPlan plan_src(const delrec_layer* ly) {
   SrcPlan p;
-  const int TB = ly->T * ly->B;
-  const int cb = cdiv(ly->N, 32);
-  int splits = std::max(1, std::min(cdiv(2 * kSMs, cb), cdiv(TB, 256)));
-  p.rows_per_split = cdiv(TB, splits);
-  p.splits = cdiv(TB, p.rows_per_split);
+  p.splits = cdiv(ly->B, 8);   // one partial row per chunk of 8 samples
   return p;
 }
 
@@ -546,6 +543,120 @@ static int dense_dw(const delrec_layer* ly, const float* gr, const float* z, int
   }
   if (nk > 1) {
     k_pick_by_offset<<<grid_for(nn, 256), 256, 0, st>>>(N, offT, P, dW);
+    DR_LAUNCHED();
+  }
+  return DELREC_OK;
+}
+
+// ---- feedforward projection on tensor cores (linear.cuh) ------------------------
+struct LinPlan {
+  int Kp, Np, pf, nbx;   // padded widths, forward blocks, backward x pieces
+};
+static LinPlan plan_linear(int K, int N, int x_binary) {
+  LinPlan p;
+  p.Kp = (K + 1 + 7) / 8 * 8;
+  p.Np = (N + 7) / 8 * 8;
+  p.pf = x_binary ? 3 : 6;
+  p.nbx = x_binary ? 1 : 3;
+  return p;
+}
+static size_t linear_fwd_ws(int M, int K, int N, int xb) {
+  const LinPlan p = plan_linear(K, N, xb);
+  Carve c(nullptr, (size_t)-1);
+  c.take<__nv_bfloat16>((size_t)M * p.pf * p.Kp);
+  c.take<__nv_bfloat16>((size_t)N * p.pf * p.Kp);
+  c.take<unsigned char>(kCublasWs);
+  return c.off;
+}
+static size_t linear_bwd_ws(int M, int K, int N, int xb) {
+  const LinPlan p = plan_linear(K, N, xb);
+  Carve c(nullptr, (size_t)-1);
+  c.take<__nv_bfloat16>((size_t)M * p.nbx * p.Kp);
+  c.take<__nv_bfloat16>((size_t)M * 6 * p.Np);
+  c.take<__nv_bfloat16>((size_t)6 * p.Np * p.Kp);
+  c.take<float>((size_t)3 * p.Np * p.Kp);
+  c.take<unsigned char>(kCublasWs);
+  return c.off;
+}
+static int gemm_bf16(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k,
+                     const void* A, int lda, const void* B, int ldb, float beta, float* C, int ldc) {
+  const float one = 1.f;
+  const cublasStatus_t e = cublasGemmEx(h, ta, tb, m, n, k, &one, A, CUDA_R_16BF, lda, B, CUDA_R_16BF, ldb,
+                                        &beta, C, CUDA_R_32F, ldc, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+  if (e != CUBLAS_STATUS_SUCCESS) {
+    fprintf(stderr, "delrec_b200: cublasGemmEx failed (%d)\n", (int)e);
+    return DELREC_ERR_CUDA;
+  }
+  return DELREC_OK;
+}
+static int cublas_on(cublasHandle_t* h, void* cws, cudaStream_t st) {
+  int rc = cublas_for_device(h);
+  if (rc) return rc;
+  if (cublasSetStream(*h, st) != CUBLAS_STATUS_SUCCESS) return DELREC_ERR_CUDA;
+  if (cublasSetWorkspace(*h, cws, kCublasWs) != CUBLAS_STATUS_SUCCESS) return DELREC_ERR_CUDA;
+  return DELREC_OK;
+}
+
+static int run_linear_forward(int M, int K, int N, const float* x, const float* W, const float* bias, int xb,
+                              float* out, void* ws, size_t wsb, cudaStream_t st) {
+  if (M <= 0 || K <= 0 || N <= 0 || !x || !W || !out) return DELREC_ERR_ARG;
+  if (((uintptr_t)ws & 255) != 0 || wsb < linear_fwd_ws(M, K, N, xb)) return DELREC_ERR_WORKSPACE;
+  const LinPlan p = plan_linear(K, N, xb);
+  Carve c(ws, wsb);
+  __nv_bfloat16* X = c.take<__nv_bfloat16>((size_t)M * p.pf * p.Kp);
+  __nv_bfloat16* Wp = c.take<__nv_bfloat16>((size_t)N * p.pf * p.Kp);
+  void* cws = c.take<unsigned char>(kCublasWs);
+  if (!c.ok) return DELREC_ERR_WORKSPACE;
+  k_pack_rows<<<grid_for((size_t)M * p.Kp, 256), 256, 0, st>>>(M, K, p.Kp, x, K, nullptr, 1, p.pf,
+                                                               xb ? kPatSpike3 : kPatReal6, xb, X);
+  DR_LAUNCHED();
+  k_pack_rows<<<grid_for((size_t)N * p.Kp, 256), 256, 0, st>>>(N, K, p.Kp, W, K, bias, 0, p.pf,
+                                                               xb ? kPatW3 : kPatW6, 0, Wp);
+  DR_LAUNCHED();
+  cublasHandle_t h;
+  int rc = cublas_on(&h, cws, st);
+  if (rc) return rc;
+  // column-major: out^T (N x M) = W'^T-view (N x P*Kp) . X'^T-view (P*Kp x M)
+  return gemm_bf16(h, CUBLAS_OP_T, CUBLAS_OP_N, N, M, p.pf * p.Kp, Wp, p.pf * p.Kp, X, p.pf * p.Kp, 0.f,
+                   out, N);
+}
+
+static int run_linear_backward(int M, int K, int N, const float* x, const float* W, const float* gout, int xb,
+                               float* dx, float* dW, float* dbias, void* ws, size_t wsb, cudaStream_t st) {
+  if (M <= 0 || K <= 0 || N <= 0 || !gout || (dx && !W) || ((dW || dbias) && !x)) return DELREC_ERR_ARG;
+  if (((uintptr_t)ws & 255) != 0 || wsb < linear_bwd_ws(M, K, N, xb)) return DELREC_ERR_WORKSPACE;
+  const LinPlan p = plan_linear(K, N, xb);
+  Carve c(ws, wsb);
+  __nv_bfloat16* X = c.take<__nv_bfloat16>((size_t)M * p.nbx * p.Kp);
+  __nv_bfloat16* G = c.take<__nv_bfloat16>((size_t)M * 6 * p.Np);
+  __nv_bfloat16* Wt = c.take<__nv_bfloat16>((size_t)6 * p.Np * p.Kp);
+  float* D = c.take<float>((size_t)3 * p.Np * p.Kp);
+  void* cws = c.take<unsigned char>(kCublasWs);
+  if (!c.ok) return DELREC_ERR_WORKSPACE;
+  k_pack_rows<<<grid_for((size_t)M * p.Np, 256), 256, 0, st>>>(M, N, p.Np, gout, N, nullptr, 0, 6, kPatReal6, 0,
+                                                               G);
+  DR_LAUNCHED();
+  cublasHandle_t h;
+  int rc = cublas_on(&h, cws, st);
+  if (rc) return rc;
+  if (dx) {
+    k_pack_wt<<<grid_for((size_t)p.Np * p.Kp, 256), 256, 0, st>>>(N, K, p.Np, p.Kp, W, kPatW6, 6, Wt);
+    DR_LAUNCHED();
+    // column-major: dx^T (K x M) = W''-view (K x 6Np) . G'-view (6Np x M)
+    rc = gemm_bf16(h, CUBLAS_OP_N, CUBLAS_OP_N, K, M, 6 * p.Np, Wt, p.Kp, G, 6 * p.Np, 0.f, dx, K);
+    if (rc) return rc;
+  }
+  if (dW || dbias) {
+    k_pack_rows<<<grid_for((size_t)M * p.Kp, 256), 256, 0, st>>>(M, K, p.Kp, x, K, nullptr, 1, p.nbx,
+                                                                 kPatDistinct3, xb, X);
+    DR_LAUNCHED();
+    // column-major: D (Kp x 3Np) = sum_a X_a-view (Kp x M) . G'-view^T (M x (3-a)Np)
+    for (int a = 0; a < p.nbx; ++a) {
+      rc = gemm_bf16(h, CUBLAS_OP_N, CUBLAS_OP_T, p.Kp, (3 - a) * p.Np, M, X + (size_t)a * p.Kp, p.nbx * p.Kp, G,
+                     6 * p.Np, a == 0 ? 0.f : 1.f, D, p.Kp);
+      if (rc) return rc;
+    }
+    k_linear_dw_reduce<<<grid_for((size_t)N * (K + 1), 256), 256, 0, st>>>(N, K, p.Np, p.Kp, D, dW, dbias);
     DR_LAUNCHED();
   }
   return DELREC_OK;
@@ -718,7 +829,7 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
   const bool need_src = g->dbias || (kind != DELREC_SYNAPTIC && (g->dd || g->ds));
   if (need_src) {
     SrcArgs sa{};
-    sa.T = T; sa.B = B; sa.N = N; sa.TAPS = bp.TAPS; sa.rows_per_split = sp.rows_per_split;
+    sa.T = T; sa.B = B; sa.N = N; sa.TAPS = bp.TAPS;
     sa.gr = gr; sa.gz = kind != DELREC_SYNAPTIC ? gz : nullptr; sa.y = y; sa.tap_l0 = tl0; sa.tap_nt = tnt;
     sa.part = spart;
     sa.MM = bp.MM;
@@ -824,6 +935,22 @@ int delrec_hybrid_backward(const delrec_layer* ly, const delrec_lif* lif, const 
                            const float* s, const float* keep, const delrec_grads* g, void* ws, size_t wsb,
                            void* stream) {
   return run_backward(ly, DELREC_HYBRID, lif, gy, u, y, W, base, offsets, s, keep, g, ws, wsb, (cudaStream_t)stream);
+}
+
+size_t delrec_linear_forward_workspace(int M, int K, int N, int x_binary) {
+  return (M > 0 && K > 0 && N > 0) ? linear_fwd_ws(M, K, N, x_binary ? 1 : 0) : 0;
+}
+size_t delrec_linear_backward_workspace(int M, int K, int N, int x_binary) {
+  return (M > 0 && K > 0 && N > 0) ? linear_bwd_ws(M, K, N, x_binary ? 1 : 0) : 0;
+}
+int delrec_linear_forward(int M, int K, int N, const float* x, const float* W, const float* bias, int x_binary,
+                          float* out, void* ws, size_t wsb, void* stream) {
+  return run_linear_forward(M, K, N, x, W, bias, x_binary ? 1 : 0, out, ws, wsb, (cudaStream_t)stream);
+}
+int delrec_linear_backward(int M, int K, int N, const float* x, const float* W, const float* gout, int x_binary,
+                           float* dx, float* dW, float* dbias, void* ws, size_t wsb, void* stream) {
+  return run_linear_backward(M, K, N, x, W, gout, x_binary ? 1 : 0, dx, dW, dbias, ws, wsb,
+                             (cudaStream_t)stream);
 }
 
 int delrec_hybrid_delay_grad(int N, int LM, const float* C, const float* W, const float* d, float sigma,

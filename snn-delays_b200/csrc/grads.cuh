@@ -175,10 +175,15 @@ __global__ void k_colsum(const float* __restrict__ m, int R, int C, float* __res
   out[c] = v;
 }
 
-// Per-neuron reductions.  Block = 32 neurons x 8 row groups; grid.y splits the rows.
-// part layout per split: [N][TAPS + 1]  (TAPS dmask sums, then the gr sum)
+// Per-neuron reductions.  Block = 32 neurons (lanes) x 8 samples (warps); grid.y runs
+// over chunks of 8 samples and each block writes one partial row per neuron.
+// part layout per chunk: [N][TAPS + 1]  (TAPS dmask sums, then the gr sum)
+// Each thread walks its (sample, neuron) through time once: gr and y are read once,
+// coalesced over neurons.  y holds the layer's spikes, so
+//   dmask[n][j] = sum_{t,b} gz_m[t,b,n] y[t-l_j,b,n] = sum_{(t',b): y != 0} y[t',b,n] gz_m[t'+l_j,b,n]
+// reads gz only at the spike times (a few percent of the elements).
 struct SrcArgs {
-  int T, B, N, TAPS, rows_per_split;
+  int T, B, N, TAPS;
   int MM;               // hybrid: a tap at base lag l <= 0 pairs with gz_{1-l}
   const float* gr;
   const float* gz;      // null: only db
@@ -191,39 +196,58 @@ struct SrcArgs {
 template <int TAPSMAX>
 __global__ void __launch_bounds__(256) k_source_reduce(SrcArgs a) {
   __shared__ float sred[8][32][TAPSMAX + 1];
-  const int lane = threadIdx.x & 31, rg = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int n = blockIdx.x * 32 + lane;
-  const int N = a.N, B = a.B, TB = a.T * a.B;
+  const int b = blockIdx.y * 8 + w;
+  const int N = a.N, B = a.B, T = a.T;
   float dm[TAPSMAX];
   float sg = 0.f;
 #pragma unroll
   for (int j = 0; j < TAPSMAX; ++j) dm[j] = 0.f;
   int lo = 1, nt = 0;
   if (n < N && a.gz) { lo = a.tap_l0[n]; nt = a.tap_nt[n]; }
-  const int r0 = blockIdx.y * a.rows_per_split, r1 = min(TB, r0 + a.rows_per_split);
-  if (n < N) {
-    for (int r = r0 + rg; r < r1; r += 8) {
-      const size_t idx = (size_t)r * N + n;
-      sg += a.gr[idx];
-      if (a.gz) {
-        const int t = r / B;
-        const size_t TBN = (size_t)TB * N;
+  if (n < N && b < B) {
+    const size_t step = (size_t)B * N;
+    const size_t TBN = (size_t)T * step;
+    const size_t base = (size_t)b * N + n;
+    const float* gp = a.gr + base;
+    const float* yp = a.y + base;
+    const bool want_y = a.gz != nullptr;
+    auto spike = [&](int tp, float yv) {
 #pragma unroll
-        for (int j = 0; j < TAPSMAX; ++j) {
-          const int l = lo + j;
-          const int m = l < 1 ? 1 - l : 0;
-          if (j < nt && m <= a.MM && t - l >= 0 && t - l < a.T)
-            dm[j] = fmaf(a.gz[(size_t)m * TBN + idx],
-                         a.y[(size_t)((long long)idx - (long long)l * B * N)], dm[j]);
-        }
+      for (int j = 0; j < TAPSMAX; ++j) {
+        const int l = lo + j;
+        const int tt = tp + l;
+        const int m = l < 1 ? 1 - l : 0;
+        if (j < nt && m <= a.MM && tt >= 0 && tt < T)
+          dm[j] = fmaf(__ldg(a.gz + (size_t)m * TBN + (size_t)tt * step + base), yv, dm[j]);
       }
+    };
+    int t = 0;
+    for (; t + 4 <= T; t += 4) {
+      float g[4], yv[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        g[q] = __ldcs(gp + (size_t)(t + q) * step);
+        yv[q] = want_y ? __ldcs(yp + (size_t)(t + q) * step) : 0.f;
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        sg += g[q];
+        if (yv[q] != 0.f) spike(t + q, yv[q]);
+      }
+    }
+    for (; t < T; ++t) {
+      sg += __ldcs(gp + (size_t)t * step);
+      const float yv = want_y ? __ldcs(yp + (size_t)t * step) : 0.f;
+      if (yv != 0.f) spike(t, yv);
     }
   }
 #pragma unroll
-  for (int j = 0; j < TAPSMAX; ++j) sred[rg][lane][j] = dm[j];
-  sred[rg][lane][TAPSMAX] = sg;
+  for (int j = 0; j < TAPSMAX; ++j) sred[w][lane][j] = dm[j];
+  sred[w][lane][TAPSMAX] = sg;
   __syncthreads();
-  if (rg == 0 && n < N) {
+  if (w == 0 && n < N) {
     float* out = a.part + ((size_t)blockIdx.y * N + n) * (a.TAPS + 1);
     for (int j = 0; j < a.TAPS; ++j) {
       float v = 0.f;

@@ -1,0 +1,107 @@
+// Feedforward projection out = x W^T + bias (torch.nn.Linear layout, W (N,K)) on bf16
+// tensor cores with fp32 accuracy.
+//
+// Every fp32 operand v is split exactly into three bf16 pieces v = p0 + p1 + p2
+// (p0 = bf16(v), p1 = bf16(v - p0), p2 = bf16(v - p0 - p1); each difference is exact in
+// fp32 and 3 x 8 significand bits cover fp32's 24).  A product a.b is then the sum of
+// the piece products a_i.b_j with i + j <= 2 (six products; the dropped ones are below
+// 2^-24 relative), accumulated in fp32 by the tensor cores.  Operands in {0, 1} (spike
+// trains) are exact in one bf16 piece, so a product with them needs three products only.
+//
+// The piece products of one output are laid side by side along the reduction dimension,
+// so each is ONE plain GEMM (cuBLAS, bf16 in, fp32 accumulate):
+//   forward   out (M,N) = X'(M, P*Kp) . W'(N, P*Kp)^T
+//   real x:   X' blocks [x0 x1 x2 x0 x1 x0], W' blocks [W0 W0 W0 W1 W1 W2]  (P = 6)
+//   spikes:   X' blocks [x  x  x ],          W' blocks [W0 W1 W2]           (P = 3)
+//   the bias rides along as column K of every block: 1 in the x0 (spike: x) blocks, the
+//   matching bias piece in W', so the GEMM returns x W^T + bias;
+//   input gradient  dx (M,K) = G'(M, 6*Np) . W''(6*Np, Kp),
+//     G' blocks [g0 g1 g2 g0 g1 g0] of gout, W'' row blocks [W0 W0 W0 W1 W1 W2];
+//   weight gradient D (3*Np, Kp) = sum_a x_a^T G'[:, 0 : (3-a)*Np]  (one GEMM for spikes,
+//     three for real x), then dW = D[0:N] + D[Np:Np+N] + D[2Np:2Np+N] and dbias = its
+//     column K.
+// Kp = roundup(K + 1, 8) and Np = roundup(N, 8) keep every bf16 row 16-byte aligned.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+
+namespace delrec {
+
+struct Pieces3 {
+  __nv_bfloat16 p[3];
+};
+__device__ __forceinline__ Pieces3 split3(float v) {
+  Pieces3 r;
+  r.p[0] = __float2bfloat16_rn(v);
+  const float r1 = __fsub_rn(v, __bfloat162float(r.p[0]));
+  r.p[1] = __float2bfloat16_rn(r1);
+  const float r2 = __fsub_rn(r1, __bfloat162float(r.p[1]));
+  r.p[2] = __float2bfloat16_rn(r2);
+  return r;
+}
+
+// Block patterns (piece index of block q), two bits per block.
+constexpr unsigned kPatReal6 = (0u << 0) | (1u << 2) | (2u << 4) | (0u << 6) | (1u << 8) | (0u << 10);
+constexpr unsigned kPatW6 = (0u << 0) | (0u << 2) | (0u << 4) | (1u << 6) | (1u << 8) | (2u << 10);
+constexpr unsigned kPatSpike3 = 0u;                                  // x, x, x
+constexpr unsigned kPatW3 = (0u << 0) | (1u << 2) | (2u << 4);      // W0, W1, W2
+constexpr unsigned kPatDistinct3 = (0u << 0) | (1u << 2) | (2u << 4);
+
+// out[r][q*Wd + c] = piece pat(q) of
+//   src[r*lds + c]                      c <  K
+//   extra ? extra[r] : (ones ? 1 : 0)   c == K  (the pieces of 1 are 1, 0, 0)
+//   0                                   K < c < Wd
+// for rows r < R.  binary != 0: values of src must be 0 or 1 (else ST_SHAPE is set).
+__global__ void k_pack_rows(int R, int K, int Wd, const float* __restrict__ src, int lds,
+                            const float* __restrict__ extra, int ones, int nb, unsigned pat,
+                            int binary, __nv_bfloat16* __restrict__ out) {
+  const size_t total = (size_t)R * Wd;
+  const size_t row_out = (size_t)nb * Wd;
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(e / Wd), c = (int)(e % Wd);
+    float v = 0.f;
+    if (c < K) {
+      v = src[(size_t)r * lds + c];
+      if (binary && !(v == 0.f || v == 1.f)) flag_status(ST_SHAPE);
+    } else if (c == K) {
+      v = extra ? extra[r] : (ones ? 1.f : 0.f);
+    }
+    const Pieces3 p = split3(v);
+    __nv_bfloat16* o = out + (size_t)r * row_out + c;
+#pragma unroll 1
+    for (int q = 0; q < nb; ++q) o[(size_t)q * Wd] = p.p[(pat >> (2 * q)) & 3];
+  }
+}
+
+// W''[q*Np + n][c] = piece pat(q) of W[n*K + c] (c < K, n < N), else 0.   (6*Np rows, Kp cols)
+__global__ void k_pack_wt(int N, int K, int Np, int Kp, const float* __restrict__ W, unsigned pat, int nb,
+                          __nv_bfloat16* __restrict__ out) {
+  const size_t total = (size_t)Np * Kp;
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+    const int n = (int)(e / Kp), c = (int)(e % Kp);
+    const float v = (n < N && c < K) ? W[(size_t)n * K + c] : 0.f;
+    const Pieces3 p = split3(v);
+#pragma unroll 1
+    for (int q = 0; q < nb; ++q) out[((size_t)q * Np + n) * Kp + c] = p.p[(pat >> (2 * q)) & 3];
+  }
+}
+
+// dW[n*K + c] = D[n][c] + D[Np+n][c] + D[2Np+n][c];  dbias[n] = the same at c = K.
+// D is (3*Np, Kp) row-major (the column-major Kp x 3Np GEMM output).
+__global__ void k_linear_dw_reduce(int N, int K, int Np, int Kp, const float* __restrict__ D,
+                                   float* __restrict__ dW, float* __restrict__ dbias) {
+  const size_t total = (size_t)N * (K + 1);
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+    const int n = (int)(e / (K + 1)), c = (int)(e % (K + 1));
+    const float v = D[(size_t)n * Kp + c] + D[((size_t)Np + n) * Kp + c] + D[((size_t)2 * Np + n) * Kp + c];
+    if (c < K) {
+      if (dW) dW[(size_t)n * K + c] = v;
+    } else if (dbias) {
+      dbias[n] = v;
+    }
+  }
+}
+
+}  // namespace delrec

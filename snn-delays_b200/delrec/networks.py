@@ -18,6 +18,7 @@ import torch
 
 from .dcls import Dcls1d
 from .delay_layers import axonal_recdel, common_recdel, synaptic_recdel
+from .linear import Linear
 from .neuron import BatchNorm1d, Dropout
 
 
@@ -64,6 +65,14 @@ class spike_registrator(torch.nn.Module):
         return x
 
 
+def _spike_input(config, idx):
+    """The input of the idx-th projection is a spike train (0/1) when a spiking layer
+    feeds it directly; the first projection's data is tested per call (None)."""
+    if idx == 0:
+        return None
+    return False if config.use_batch_norm else True
+
+
 def _init_ff(m, config):
     if isinstance(m, torch.nn.Linear):
         if config.init_ff_weights == "kaiming":
@@ -80,15 +89,16 @@ class SNN(torch.nn.Module):
         assert config.dataset in ["SSC", "PSMNIST", "HAR", "AL", "MG", "MEM"], "Unsupported SNN dataset."
         self.config = config
         layers, dim = [], config.input_size
-        for width in config.hidden_layers:
-            layers.append(torch.nn.Linear(dim, width, bias=config.bias))
+        for idx, width in enumerate(config.hidden_layers):
+            layers.append(Linear(dim, width, bias=config.bias, binary_input=_spike_input(config, idx)))
             dim = width
             layers.append(Dropout(config.feedforward_dropout_rate, step_mode="m"))
             layers.append(_lif(config))
             layers.append(spike_registrator())
             if config.use_batch_norm:
                 layers.append(modified_batchnorm(width, step_mode="m"))
-        layers.append(torch.nn.Linear(dim, config.output_size, bias=config.bias))
+        layers.append(Linear(dim, config.output_size, bias=config.bias,
+                             binary_input=_spike_input(config, len(config.hidden_layers))))
         self.layers = torch.nn.Sequential(*layers)
         self.init_weights()
 
@@ -104,7 +114,7 @@ class SNN(torch.nn.Module):
 def _recurrent_stack(config, recurrent_cls):
     layers, dim = [], config.input_size
     for idx, width in enumerate(config.hidden_layers):
-        layers.append(torch.nn.Linear(dim, width, bias=config.bias))
+        layers.append(Linear(dim, width, bias=config.bias, binary_input=_spike_input(config, idx)))
         dim = width
         layers.append(Dropout(config.feedforward_dropout_rate, step_mode="m"))
         last = idx == len(config.hidden_layers) - 1
@@ -115,7 +125,8 @@ def _recurrent_stack(config, recurrent_cls):
         layers.append(spike_registrator())
         if config.use_batch_norm:
             layers.append(modified_batchnorm(width, step_mode="m"))
-    layers.append(torch.nn.Linear(dim, config.output_size, bias=config.bias))
+    layers.append(Linear(dim, config.output_size, bias=config.bias,
+                         binary_input=_spike_input(config, len(config.hidden_layers))))
     return torch.nn.Sequential(*layers)
 
 
@@ -234,7 +245,7 @@ class SNN_synaptic_feedforward_delays(SNN):
         layers, dim = [], config.input_size
         for idx, width in enumerate(config.hidden_layers):
             if config.no_delay_in_first_layer and idx == 0:
-                layers.append(torch.nn.Linear(dim, width, bias=config.bias))
+                layers.append(Linear(dim, width, bias=config.bias))
             else:
                 layers.append(dcls_module(config, dim, width, groups=1))
             dim = width
@@ -244,7 +255,7 @@ class SNN_synaptic_feedforward_delays(SNN):
             if config.use_batch_norm:
                 layers.append(modified_batchnorm(width, step_mode="m"))
         if config.no_delay_in_last_layer:
-            layers.append(torch.nn.Linear(dim, config.output_size, bias=config.bias))
+            layers.append(Linear(dim, config.output_size, bias=config.bias))
         else:
             layers.append(dcls_module(config, dim, config.output_size, groups=1))
         self.layers = torch.nn.Sequential(*layers)
@@ -291,11 +302,11 @@ class SNN_axonal_feedforward_delays(SNN_synaptic_feedforward_delays):
 
     def _delay_stage(self, in_dim, out_dim, delayed):
         if not delayed:
-            return [torch.nn.Linear(in_dim, out_dim, bias=self.config.bias)]
+            return [Linear(in_dim, out_dim, bias=self.config.bias)]
         dc = copy(self.config)
         dc.bias = False
         return [dcls_module(dc, in_channels=in_dim, out_channels=in_dim, groups=in_dim),
-                torch.nn.Linear(in_dim, out_dim, bias=self.config.bias)]
+                Linear(in_dim, out_dim, bias=self.config.bias)]
 
     def init_weights(self):
         for m in self.layers:
@@ -319,7 +330,7 @@ class SNN_recurrent_and_feedforward_delays(SNN_synaptic_feedforward_delays, SNN_
         layers, dim = [], config.input_size
         for idx, width in enumerate(config.hidden_layers):
             if config.no_delay_in_first_layer and idx == 0:
-                layers.append(torch.nn.Linear(dim, width, bias=config.bias))
+                layers.append(Linear(dim, width, bias=config.bias))
             else:
                 layers.append(dcls_module(config, dim, width, groups=1))
             dim = width
@@ -329,7 +340,7 @@ class SNN_recurrent_and_feedforward_delays(SNN_synaptic_feedforward_delays, SNN_
             if config.use_batch_norm:
                 layers.append(modified_batchnorm(width, step_mode="m"))
         if config.no_delay_in_last_layer:
-            layers.append(torch.nn.Linear(dim, config.output_size, bias=config.bias))
+            layers.append(Linear(dim, config.output_size, bias=config.bias))
         else:
             layers.append(dcls_module(config, dim, config.output_size, groups=1))
         self.layers = torch.nn.Sequential(*layers)
@@ -377,13 +388,13 @@ class SNN_axonal_recurrent_and_feedforward_delays(SNN_recurrent_and_feedforward_
 
     def _projection(self, inputs, outputs, delayed):
         if not delayed:
-            return [torch.nn.Linear(inputs, outputs, bias=self.config.bias)]
+            return [Linear(inputs, outputs, bias=self.config.bias)]
         if not self.axonal_feedforward:
             return [dcls_module(self.config, inputs, outputs, groups=1)]
         dc = copy(self.config)
         dc.bias = False
         return [dcls_module(dc, inputs, inputs, groups=inputs),
-                torch.nn.Linear(inputs, outputs, bias=self.config.bias)]
+                Linear(inputs, outputs, bias=self.config.bias)]
 
     def init_weights(self):
         SNN_synaptic_feedforward_delays.init_weights(self)
