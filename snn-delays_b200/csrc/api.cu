@@ -11,6 +11,7 @@
 
 #include "backward.cuh"
 #include "backward_hybrid.cuh"
+#include "backward_hybrid64.cuh"
 #include "dense.cuh"
 #include "forward.cuh"
 #include "grads.cuh"
@@ -365,6 +366,49 @@ static int launch_hyb_t(const HybArgs& a, const HybPlan& h, cudaStream_t st) {
   return DELREC_OK;
 }
 
+// Hybrid reverse scan with 64-sample tiles and deferred synapse sums
+// (backward_hybrid64.cuh): cooperative single wave, every base tap at lag >= 1 (MM = 0),
+// K <= 8, N <= 512 (gr of a tile staged in shared memory), at most 8 taps per source.
+struct Hyb64Plan {
+  bool ok;
+  int CS, tiles, CAPS, KMAX;
+  size_t smem;
+};
+static constexpr int kH64Taps = 8;
+static Hyb64Plan plan_hybrid64(const delrec_layer* ly, const BwdPlan& bp) {
+  Hyb64Plan h{};
+  h.ok = false;
+  if (ly->kind != DELREC_HYBRID || bp.MM != 0 || ly->K > 8 || ly->N > 512 || bp.TAPS > kH64Taps) return h;
+  if (ly->B <= 32) return h;   // a 32-sample tile (k_bwd_hybrid) wastes no lanes there
+  h.CS = cdiv(ly->N, kH64NT);
+  h.tiles = cdiv(ly->B, kH64BT);
+  if (h.CS * h.tiles > kSMs) return h;
+  h.CAPS = ((ly->N + 7 * (ly->K + 1)) + 7) / 8 * 8;
+  h.KMAX = ly->K <= 4 ? 6 : 10;
+  h.smem = hyb64_smem_plan(ly->N, h.CAPS, ly->K, bp.TAPS, h.KMAX).total;
+  h.ok = h.smem <= kSmemLimit;
+  return h;
+}
+
+template <int KMAX>
+static int launch_hyb64_t(const Hyb64Args& a, const Hyb64Plan& h, cudaStream_t st) {
+  auto kern = k_bwd_hybrid64<KMAX, kH64Taps>;
+  int rc = set_smem(kern, h.smem);
+  if (rc) return rc;
+  int per_sm = 0;
+  DR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kH64Threads, h.smem));
+  if (per_sm < 1 || h.CS * h.tiles > per_sm * kSMs) return DELREC_ERR_UNSUPPORTED;
+  DR_CUDA(cudaMemsetAsync(a.arrive, 0, sizeof(unsigned int) * h.tiles, st));
+  Hyb64Args ac = a;
+  void* args[] = {(void*)&ac};
+  scan_mark(0, st);
+  DR_CUDA(cudaLaunchCooperativeKernel((const void*)kern, dim3(h.CS * h.tiles), dim3(kH64Threads), args, h.smem,
+                                      st));
+  scan_mark(1, st);
+  ++g_launches;
+  return DELREC_OK;
+}
+
 template <int MODE, int BT, int PPT>
 static int launch_bwd_t(const BwdArgs& a, const BwdPlan& p, cudaStream_t st) {
   auto kern = k_bwd<MODE, BT, PPT>;
@@ -681,7 +725,7 @@ static size_t backward_ws(const delrec_layer* ly, int kind) {
     c.take<int>(N * (size_t)(bp.NKEY + 1));
   }
   if (kind == DELREC_HYBRID) {
-    c.take<float>((size_t)2 * cdiv(ly->B, 32) * N * 32);   // gr exchange (cooperative mode)
+    c.take<float>((size_t)2 * cdiv(ly->B, 64) * N * 64);   // gr exchange (cooperative modes)
     c.take<unsigned int>((size_t)cdiv(ly->B, 32));         // arrival counters
   }
   const int parts = kind == DELREC_SYNAPTIC ? 3 : 1;
@@ -740,12 +784,13 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
   int2* ent = nullptr;
   int* boff = nullptr;
   const HybPlan hp = plan_hybrid_fast(ly, bp);
+  const Hyb64Plan h64 = plan_hybrid64(ly, bp);
   if (kind != DELREC_AXONAL) {
     ent = c.take<int2>((size_t)N * bp.CAP);
     boff = c.take<int>((size_t)N * (bp.NKEY + 1));
     const int nth = std::min(256, ((N + 31) / 32) * 32);
     const size_t sm = (size_t)nth * 8;
-    const int padm = hp.ok ? 8 : bp.PADM;
+    const int padm = (hp.ok || h64.ok) ? 8 : bp.PADM;
     if (kind == DELREC_HYBRID)
       k_buckets<1><<<N, nth, sm, st>>>(N, bp.NKEY, bp.CAP, padm, W, offT, nullptr, s, ent, boff);
     else
@@ -762,10 +807,18 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
   float* grx = nullptr;
   unsigned int* arrive = nullptr;
   if (kind == DELREC_HYBRID) {
-    grx = c.take<float>((size_t)2 * cdiv(B, 32) * N * 32);
+    grx = c.take<float>((size_t)2 * cdiv(B, 64) * N * 64);
     arrive = c.take<unsigned int>((size_t)cdiv(B, 32));
   }
-  if (hp.ok) {
+  if (h64.ok) {
+    Hyb64Args h{};
+    h.T = T; h.B = B; h.N = N; h.K = ly->K; h.CS = h64.CS; h.TAPS = bp.TAPS; h.CAPS = h64.CAPS; h.CAP = bp.CAP;
+    h.gy = gy; h.u = u; h.keep = ly->has_keep ? keep : nullptr;
+    h.tap_l0 = tl0; h.tap_nt = tnt; h.tap_w = tw; h.ent = ent; h.boff = boff;
+    h.dx = g->dx; h.gr = gr; h.gz = gz; h.lif = a.lif;
+    h.grx = grx; h.arrive = arrive; h.spin_limit = 1ll << 22;
+    rc = h64.KMAX == 6 ? launch_hyb64_t<6>(h, h64, st) : launch_hyb64_t<10>(h, h64, st);
+  } else if (hp.ok) {
     HybArgs h{};
     h.grx = grx; h.arrive = arrive; h.spin_limit = 1ll << 22;
     h.T = T; h.B = B; h.N = N; h.K = ly->K; h.CS = hp.CS; h.NT = hp.NT; h.TAPS = bp.TAPS; h.MM = bp.MM;

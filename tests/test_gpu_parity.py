@@ -123,6 +123,9 @@ SHAPES = [
     ("hybrid", 40, 36, 128, 0.0, False, False, False, 8.0, 4),
     ("hybrid", 25, 40, 512, 0.0, False, True, False, 25.0, 8),
     ("hybrid", 20, 9, 33, 1.0, False, False, True, 5.0, 3),
+    # 64-sample tiles with deferred sums: ragged batch tile and neuron slice
+    ("hybrid", 30, 100, 200, 0.0, False, True, True, 20.0, 8),
+    ("hybrid", 24, 70, 512, 0.0, False, False, False, 3.0, 2),
 ]
 
 
