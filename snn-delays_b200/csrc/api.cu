@@ -131,8 +131,10 @@ static FwdPlan plan_forward(const delrec_layer* ly, int kind) {
     p.smem = (size_t)p.R * p.NW * 4 + (size_t)N * (2 + p.TAPS) * 4 + (size_t)N * 8;
   } else {
     const size_t ring = (size_t)ly->L * N * 4;
-    p.ring_smem = (ring + (size_t)N * 4 <= 160 * 1024) ? 1 : 0;
-    p.smem = (p.ring_smem ? ring : 0) + (size_t)N * 4;
+    // event list, s, base; hybrid: the base's tap table
+    const size_t rest = (size_t)N * 4 * 3 + (kind == DELREC_HYBRID ? (size_t)N * 4 * (2 + p.TAPS) : 0);
+    p.ring_smem = (ring + rest <= 160 * 1024) ? 1 : 0;
+    p.smem = (p.ring_smem ? ring : 0) + rest;
   }
   return p;
 }
@@ -172,6 +174,7 @@ static size_t forward_ws(const delrec_layer* ly, int kind) {
     c.take<float>(N * N);                           // dT
   } else {
     c.take<uint8_t>(N * N);                         // offT
+    c.take<int>(N); c.take<int>(N); c.take<float>(N * p.TAPS);   // base taps
   }
   if (kind != DELREC_AXONAL && !p.ring_smem) c.take<float>((size_t)ly->B * ly->L * N);
   return c.off;
@@ -226,6 +229,13 @@ static int run_forward(const delrec_layer* ly, int kind, const delrec_lif* lif, 
     DR_LAUNCHED();
     a.offT = offT;
     a.base = d;
+    // base taps from lag 1-K: a base lag l' <= 0 reaches the synapses with offset >= 1-l'
+    int* l0 = c.take<int>(N);
+    int* nt = c.take<int>(N);
+    float* w = c.take<float>((size_t)N * p.TAPS);
+    k_taps<<<cdiv(N, 256), 256, 0, st>>>(d, s, N, ly->L - 1, p.TAPS, 1 - ly->K, l0, nt, w);
+    DR_LAUNCHED();
+    a.tap_l0 = l0; a.tap_nt = nt; a.tap_w = w;
   }
   if (!p.ring_smem) a.ring_g = c.take<float>((size_t)ly->B * ly->L * N);
   const bool hyb = kind == DELREC_HYBRID;
@@ -651,11 +661,11 @@ static int run_linear_forward(int M, int K, int N, const float* x, const float* 
   __nv_bfloat16* Wp = c.take<__nv_bfloat16>((size_t)N * p.pf * p.Kp);
   void* cws = c.take<unsigned char>(kCublasWs);
   if (!c.ok) return DELREC_ERR_WORKSPACE;
-  k_pack_rows<<<grid_for((size_t)M * p.Kp, 256), 256, 0, st>>>(M, K, p.Kp, x, K, nullptr, 1, p.pf,
-                                                               xb ? kPatSpike3 : kPatReal6, xb, X);
+  k_pack_rows<<<grid_for((size_t)M * p.Kp / 8, 256), 256, 0, st>>>(M, K, p.Kp, x, K, nullptr, 1, p.pf,
+                                                                   xb ? kPatSpike3 : kPatReal6, xb, X);
   DR_LAUNCHED();
-  k_pack_rows<<<grid_for((size_t)N * p.Kp, 256), 256, 0, st>>>(N, K, p.Kp, W, K, bias, 0, p.pf,
-                                                               xb ? kPatW3 : kPatW6, 0, Wp);
+  k_pack_rows<<<grid_for((size_t)N * p.Kp / 8, 256), 256, 0, st>>>(N, K, p.Kp, W, K, bias, 0, p.pf,
+                                                                   xb ? kPatW3 : kPatW6, 0, Wp);
   DR_LAUNCHED();
   cublasHandle_t h;
   int rc = cublas_on(&h, cws, st);
@@ -677,22 +687,22 @@ static int run_linear_backward(int M, int K, int N, const float* x, const float*
   float* D = c.take<float>((size_t)3 * p.Np * p.Kp);
   void* cws = c.take<unsigned char>(kCublasWs);
   if (!c.ok) return DELREC_ERR_WORKSPACE;
-  k_pack_rows<<<grid_for((size_t)M * p.Np, 256), 256, 0, st>>>(M, N, p.Np, gout, N, nullptr, 0, 6, kPatReal6, 0,
-                                                               G);
+  k_pack_rows<<<grid_for((size_t)M * p.Np / 8, 256), 256, 0, st>>>(M, N, p.Np, gout, N, nullptr, 0, 6, kPatReal6,
+                                                                   0, G);
   DR_LAUNCHED();
   cublasHandle_t h;
   int rc = cublas_on(&h, cws, st);
   if (rc) return rc;
   if (dx) {
-    k_pack_wt<<<grid_for((size_t)p.Np * p.Kp, 256), 256, 0, st>>>(N, K, p.Np, p.Kp, W, kPatW6, 6, Wt);
+    k_pack_wt<<<grid_for((size_t)p.Np * p.Kp / 8, 256), 256, 0, st>>>(N, K, p.Np, p.Kp, W, kPatW6, 6, Wt);
     DR_LAUNCHED();
     // column-major: dx^T (K x M) = W''-view (K x 6Np) . G'-view (6Np x M)
     rc = gemm_bf16(h, CUBLAS_OP_N, CUBLAS_OP_N, K, M, 6 * p.Np, Wt, p.Kp, G, 6 * p.Np, 0.f, dx, K);
     if (rc) return rc;
   }
   if (dW || dbias) {
-    k_pack_rows<<<grid_for((size_t)M * p.Kp, 256), 256, 0, st>>>(M, K, p.Kp, x, K, nullptr, 1, p.nbx,
-                                                                 kPatDistinct3, xb, X);
+    k_pack_rows<<<grid_for((size_t)M * p.Kp / 8, 256), 256, 0, st>>>(M, K, p.Kp, x, K, nullptr, 1, p.nbx,
+                                                                     kPatDistinct3, xb, X);
     DR_LAUNCHED();
     // column-major: D (Kp x 3Np) = sum_a X_a-view (Kp x M) . G'-view^T (M x (3-a)Np)
     for (int a = 0; a < p.nbx; ++a) {

@@ -126,12 +126,20 @@ __global__ void __launch_bounds__(512) k_fwd_axonal(FwdArgs a) {
 
 // --------------------------------------------------------------------------------
 // synaptic / hybrid: delay ring + spike-event scatter.   dynamic smem:
-//   ring L*N f32 (if ring_smem) | ev_o N int
+//   ring L*N f32 (if ring_smem) | ev_o N int | s N f32 | base N f32
+//   | hybrid: tap l0 N int | tap count N int | tap weights N*TAPS f32
+// The global loads of up to 8 events (W row element, delay or offset) are issued
+// together before their ring updates, so a step waits on about one L2 round trip
+// instead of one per fired source; the ring cells still receive the events in order.
+// Hybrid synapses use the integer-offset identity h(l; base_o + k) = h(l - k; base_o):
+// the source's base taps (lags l0_o + j, weights h(l0_o + j; base_o)) land k slots
+// later, so the per-synapse work is one offset byte, one weight and a few adds.
 // --------------------------------------------------------------------------------
 template <int IPT, bool HYB>
 __global__ void __launch_bounds__(512) k_fwd_synaptic(FwdArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ int s_warp[33];
+  constexpr int EB = 8;
   const int N = a.N, T = a.T, B = a.B, L = a.L, NTH = blockDim.x, tid = threadIdx.x;
   const int b = blockIdx.x;
   float* ring;
@@ -143,21 +151,44 @@ __global__ void __launch_bounds__(512) k_fwd_synaptic(FwdArgs a) {
     ring = a.ring_g + (size_t)b * L * N;
     ev_o = (int*)smem;
   }
+  float* s_s = (float*)(ev_o + N);
+  float* s_base = s_s + N;
+  int* s_l0 = (int*)(s_base + N);
+  int* s_nt = s_l0 + N;
+  float* s_tw = (float*)(s_nt + N);
   for (size_t e = tid; e < (size_t)L * N; e += NTH) ring[e] = 0.f;
+  for (int o = tid; o < N; o += NTH) {
+    s_s[o] = a.s[o];
+    s_base[o] = HYB ? a.base[o] : 0.f;
+    if (HYB) {
+      s_l0[o] = a.tap_l0[o];
+      s_nt[o] = a.tap_nt[o];
+    }
+  }
+  if (HYB)
+    for (int e = tid; e < N * a.TAPS; e += NTH) s_tw[e] = a.tap_w[e];
 
-  float v[IPT], kp[IPT], bs[IPT];
+  float v[IPT], kp[IPT], bs[IPT], xn[IPT];
 #pragma unroll
   for (int q = 0; q < IPT; ++q) {
     const int i = q * NTH + tid;
     v[q] = a.lif.v0;
     kp[q] = (a.keep && i < N) ? a.keep[(size_t)b * N + i] : 1.f;
     bs[q] = (a.bias && i < N) ? a.bias[i] : 0.f;
+    xn[q] = (i < N && T > 0) ? __ldcs(a.x + (size_t)b * N + i) : 0.f;
   }
   __syncthreads();
 
   int slot = 0;  // t mod L
   for (int t = 0; t < T; ++t) {
     const size_t rowoff = ((size_t)t * B + b) * N;
+    float xc[IPT];
+#pragma unroll
+    for (int q = 0; q < IPT; ++q) {
+      const int i = q * NTH + tid;
+      xc[q] = xn[q];
+      xn[q] = (i < N && t + 1 < T) ? __ldcs(a.x + rowoff + (size_t)B * N + i) : 0.f;
+    }
     int nev = 0;
 #pragma unroll
     for (int q = 0; q < IPT; ++q) {
@@ -168,42 +199,75 @@ __global__ void __launch_bounds__(512) k_fwd_synaptic(FwdArgs a) {
         const float rsum = *cell;
         *cell = 0.f;
         const float rec = __fmul_rn(__fadd_rn(rsum, bs[q]), kp[q]);
-        const float av = __fadd_rn(a.x[rowoff + i], rec);
+        const float av = __fadd_rn(xc[q], rec);
         const float uu = lif_charge(v[q], av, a.lif);
         sp = lif_fire(uu, a.lif);
         v[q] = lif_reset(uu, sp, a.lif);
-        a.y[rowoff + i] = sp ? 1.f : 0.f;
-        a.u[rowoff + i] = uu;
+        __stcs(a.y + rowoff + i, sp ? 1.f : 0.f);
+        __stcs(a.u + rowoff + i, uu);
       }
       nev += block_compact(sp, i, 0.f, ev_o, nullptr, nev, s_warp);
     }
     // ---- scatter the fired sources into the ring (lags 1..L-1)
-    for (int e = 0; e < nev; ++e) {
-      const int o = ev_o[e];
-      const float so = a.s[o];
-      const float bo = HYB ? a.base[o] : 0.f;
-      const float* wrow = a.WT + (size_t)o * N;
+    for (int e0 = 0; e0 < nev; e0 += EB) {
+      const int ne = min(EB, nev - e0);
+      int oo[EB];
+#pragma unroll
+      for (int j = 0; j < EB; ++j) oo[j] = j < ne ? ev_o[e0 + j] : 0;
 #pragma unroll
       for (int q = 0; q < IPT; ++q) {
         const int i = q * NTH + tid;
         if (i >= N) continue;
-        const float w = __ldg(wrow + i);
-        const float d = HYB ? __fadd_rn(bo, (float)a.offT[(size_t)o * N + i]) : __ldg(a.dT + (size_t)o * N + i);
-        const Tri tr = make_tri(d, so);
-        int lo = (int)floorf(__fsub_rn(tr.onepd, tr.s));
-        int hi = (int)ceilf(__fadd_rn(tr.onepd, tr.s));
-        lo = lo < 1 ? 1 : lo;
-        if (hi > L - 1) {
-          if (tri_clamped(tr, L) > 0.f) flag_status(ST_LAG_RANGE);
-          hi = L - 1;
+        float w[EB], dv[EB];
+#pragma unroll
+        for (int j = 0; j < EB; ++j) {
+          if (j < ne) {
+            const size_t off = (size_t)oo[j] * N + i;
+            w[j] = __ldg(a.WT + off);
+            dv[j] = HYB ? (float)a.offT[off] : __ldg(a.dT + off);
+          }
         }
-        for (int l = lo; l <= hi; ++l) {
-          const float c = tri_clamped(tr, l);
-          if (c > 0.f) {
-            int sl = slot + l;
-            if (sl >= L) sl -= L;
-            float* cell = ring + (size_t)sl * N + i;
-            *cell = __fadd_rn(*cell, __fmul_rn(w, __fdiv_rn(c, tr.s2)));
+        if (HYB) {
+#pragma unroll
+          for (int j = 0; j < EB; ++j) {
+            if (j >= ne) break;
+            const int o = oo[j];
+            const int lo = s_l0[o] + (int)dv[j], n = s_nt[o];
+            const float* hw = s_tw + (size_t)o * a.TAPS;
+            for (int q2 = 0; q2 < n; ++q2) {
+              const float h = hw[q2];
+              const int l = lo + q2;
+              if (!(h > 0.f) || l < 1) continue;
+              if (l > L - 1) { flag_status(ST_LAG_RANGE); continue; }
+              int sl = slot + l;
+              if (sl >= L) sl -= L;
+              float* cell = ring + (size_t)sl * N + i;
+              *cell = __fadd_rn(*cell, __fmul_rn(w[j], h));
+            }
+          }
+          continue;
+        }
+#pragma unroll
+        for (int j = 0; j < EB; ++j) {
+          if (j >= ne) break;
+          const int o = oo[j];
+          const float d = dv[j];
+          const Tri tr = make_tri(d, s_s[o]);
+          int lo = (int)floorf(__fsub_rn(tr.onepd, tr.s));
+          int hi = (int)ceilf(__fadd_rn(tr.onepd, tr.s));
+          lo = lo < 1 ? 1 : lo;
+          if (hi > L - 1) {
+            if (tri_clamped(tr, L) > 0.f) flag_status(ST_LAG_RANGE);
+            hi = L - 1;
+          }
+          for (int l = lo; l <= hi; ++l) {
+            const float c = tri_clamped(tr, l);
+            if (c > 0.f) {
+              int sl = slot + l;
+              if (sl >= L) sl -= L;
+              float* cell = ring + (size_t)sl * N + i;
+              *cell = __fadd_rn(*cell, __fmul_rn(w[j], __fdiv_rn(c, tr.s2)));
+            }
           }
         }
       }

@@ -54,37 +54,75 @@ constexpr unsigned kPatDistinct3 = (0u << 0) | (1u << 2) | (2u << 4);
 //   extra ? extra[r] : (ones ? 1 : 0)   c == K  (the pieces of 1 are 1, 0, 0)
 //   0                                   K < c < Wd
 // for rows r < R.  binary != 0: values of src must be 0 or 1 (else ST_SHAPE is set).
+// Wd is a multiple of 8: a thread packs 8 consecutive columns (16-byte stores).
+__device__ __forceinline__ uint32_t pack_bf16x2(__nv_bfloat16 lo, __nv_bfloat16 hi) {
+  return (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
+}
 __global__ void k_pack_rows(int R, int K, int Wd, const float* __restrict__ src, int lds,
                             const float* __restrict__ extra, int ones, int nb, unsigned pat,
                             int binary, __nv_bfloat16* __restrict__ out) {
-  const size_t total = (size_t)R * Wd;
+  const int groups = Wd >> 3;
+  const size_t total = (size_t)R * groups;
   const size_t row_out = (size_t)nb * Wd;
+  const bool vec = (lds & 3) == 0 && ((uintptr_t)src & 15) == 0;
   for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
-    const int r = (int)(e / Wd), c = (int)(e % Wd);
-    float v = 0.f;
-    if (c < K) {
-      v = src[(size_t)r * lds + c];
-      if (binary && !(v == 0.f || v == 1.f)) flag_status(ST_SHAPE);
-    } else if (c == K) {
-      v = extra ? extra[r] : (ones ? 1.f : 0.f);
+    const int r = (int)(e / groups), c0 = (int)(e % groups) * 8;
+    float v[8];
+    const float* sp = src + (size_t)r * lds + c0;
+    if (vec && c0 + 8 <= K) {
+      const float4 x0 = __ldcs((const float4*)sp), x1 = __ldcs((const float4*)sp + 1);
+      v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
+      v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+    } else {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int c = c0 + q;
+        v[q] = c < K ? sp[q] : (c == K ? (extra ? extra[r] : (ones ? 1.f : 0.f)) : 0.f);
+      }
     }
-    const Pieces3 p = split3(v);
-    __nv_bfloat16* o = out + (size_t)r * row_out + c;
+    Pieces3 p[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      if (binary && c0 + q < K && !(v[q] == 0.f || v[q] == 1.f)) flag_status(ST_SHAPE);
+      p[q] = split3(v[q]);
+    }
+    uint4* o = (uint4*)(out + (size_t)r * row_out + c0);
 #pragma unroll 1
-    for (int q = 0; q < nb; ++q) o[(size_t)q * Wd] = p.p[(pat >> (2 * q)) & 3];
+    for (int b = 0; b < nb; ++b) {
+      const int pi = (pat >> (2 * b)) & 3;
+      uint4 w;
+      w.x = pack_bf16x2(p[0].p[pi], p[1].p[pi]);
+      w.y = pack_bf16x2(p[2].p[pi], p[3].p[pi]);
+      w.z = pack_bf16x2(p[4].p[pi], p[5].p[pi]);
+      w.w = pack_bf16x2(p[6].p[pi], p[7].p[pi]);
+      o[(size_t)b * (Wd >> 3)] = w;
+    }
   }
 }
 
 // W''[q*Np + n][c] = piece pat(q) of W[n*K + c] (c < K, n < N), else 0.   (6*Np rows, Kp cols)
 __global__ void k_pack_wt(int N, int K, int Np, int Kp, const float* __restrict__ W, unsigned pat, int nb,
                           __nv_bfloat16* __restrict__ out) {
-  const size_t total = (size_t)Np * Kp;
+  const int groups = Kp >> 3;
+  const size_t total = (size_t)Np * groups;
   for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
-    const int n = (int)(e / Kp), c = (int)(e % Kp);
-    const float v = (n < N && c < K) ? W[(size_t)n * K + c] : 0.f;
-    const Pieces3 p = split3(v);
+    const int n = (int)(e / groups), c0 = (int)(e % groups) * 8;
+    Pieces3 p[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int c = c0 + q;
+      p[q] = split3((n < N && c < K) ? W[(size_t)n * K + c] : 0.f);
+    }
 #pragma unroll 1
-    for (int q = 0; q < nb; ++q) out[((size_t)q * Np + n) * Kp + c] = p.p[(pat >> (2 * q)) & 3];
+    for (int b = 0; b < nb; ++b) {
+      const int pi = (pat >> (2 * b)) & 3;
+      uint4 w;
+      w.x = pack_bf16x2(p[0].p[pi], p[1].p[pi]);
+      w.y = pack_bf16x2(p[2].p[pi], p[3].p[pi]);
+      w.z = pack_bf16x2(p[4].p[pi], p[5].p[pi]);
+      w.w = pack_bf16x2(p[6].p[pi], p[7].p[pi]);
+      *(uint4*)(out + ((size_t)b * Np + n) * Kp + c0) = w;
+    }
   }
 }
 
