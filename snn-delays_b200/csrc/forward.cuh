@@ -219,12 +219,14 @@ __global__ void __launch_bounds__(512) k_fwd_synaptic(FwdArgs a) {
         const int i = q * NTH + tid;
         if (i >= N) continue;
         float w[EB], dv[EB];
+        int kv[EB];   // hybrid integer offsets (no float round trip: conversions are quarter-rate)
 #pragma unroll
         for (int j = 0; j < EB; ++j) {
           if (j < ne) {
             const size_t off = (size_t)oo[j] * N + i;
             w[j] = __ldg(a.WT + off);
-            dv[j] = HYB ? (float)a.offT[off] : __ldg(a.dT + off);
+            if (HYB) kv[j] = a.offT[off];
+            else dv[j] = __ldg(a.dT + off);
           }
         }
         if (HYB) {
@@ -232,7 +234,7 @@ __global__ void __launch_bounds__(512) k_fwd_synaptic(FwdArgs a) {
           for (int j = 0; j < EB; ++j) {
             if (j >= ne) break;
             const int o = oo[j];
-            const int lo = s_l0[o] + (int)dv[j], n = s_nt[o];
+            const int lo = s_l0[o] + kv[j], n = s_nt[o];
             const float* hw = s_tw + (size_t)o * a.TAPS;
             for (int q2 = 0; q2 < n; ++q2) {
               const float h = hw[q2];
