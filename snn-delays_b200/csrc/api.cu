@@ -381,21 +381,29 @@ static int launch_hyb_t(const HybArgs& a, const HybPlan& h, cudaStream_t st) {
 // K <= 8, N <= 512 (gr of a tile staged in shared memory), at most 8 taps per source.
 struct Hyb64Plan {
   bool ok;
-  int CS, tiles, CAPS, KMAX;
+  int CS, tiles, CAPS, KMAX, K, NKEY, CAP;
   size_t smem;
 };
 static constexpr int kH64Taps = 8;
+// Axonal layers run the same scan as a hybrid layer whose offsets are all 0 (one bucket
+// per source holding all its synapses).
 static Hyb64Plan plan_hybrid64(const delrec_layer* ly, const BwdPlan& bp) {
   Hyb64Plan h{};
   h.ok = false;
-  if (ly->kind != DELREC_HYBRID || bp.MM != 0 || ly->K > 8 || ly->N > 512 || bp.TAPS > kH64Taps) return h;
-  if (ly->B <= 32) return h;   // a 32-sample tile (k_bwd_hybrid) wastes no lanes there
+  if (ly->kind == DELREC_SYNAPTIC) return h;
+  h.K = ly->kind == DELREC_HYBRID ? ly->K : 0;
+  if (bp.MM != 0 || h.K > 8 || ly->N > 512 || bp.TAPS > kH64Taps) return h;
+  if (ly->B <= 32) return h;   // a 32-sample tile wastes no lanes there
   h.CS = cdiv(ly->N, kH64NT);
   h.tiles = cdiv(ly->B, kH64BT);
   if (h.CS * h.tiles > kSMs) return h;
-  h.CAPS = ((ly->N + 7 * (ly->K + 1)) + 7) / 8 * 8;
-  h.KMAX = ly->K <= 4 ? 6 : 10;
-  h.smem = hyb64_smem_plan(ly->N, h.CAPS, ly->K, bp.TAPS, h.KMAX).total;
+  // small axonal layers keep the generic cluster scan (a few 64-sample blocks run slower)
+  if (ly->kind == DELREC_AXONAL && h.CS * h.tiles < 32) return h;
+  h.CAPS = ((ly->N + 7 * (h.K + 1)) + 7) / 8 * 8;
+  h.NKEY = h.K + 1;
+  h.CAP = ly->kind == DELREC_HYBRID ? bp.CAP : h.CAPS;
+  h.KMAX = h.K <= 4 ? 6 : 10;
+  h.smem = hyb64_smem_plan(ly->N, h.CAPS, h.K, bp.TAPS, h.KMAX).total;
   h.ok = h.smem <= kSmemLimit;
   return h;
 }
@@ -738,6 +746,16 @@ static size_t backward_ws(const delrec_layer* ly, int kind) {
     c.take<float>((size_t)2 * cdiv(ly->B, 64) * N * 64);   // gr exchange (cooperative modes)
     c.take<unsigned int>((size_t)cdiv(ly->B, 32));         // arrival counters
   }
+  if (kind == DELREC_AXONAL) {
+    const Hyb64Plan h64 = plan_hybrid64(ly, bp);
+    if (h64.ok) {
+      c.take<uint8_t>(N * N);                              // zero offsets
+      c.take<int2>(N * (size_t)h64.CAP);
+      c.take<int>(N * (size_t)(h64.NKEY + 1));
+      c.take<float>((size_t)2 * h64.tiles * N * 64);
+      c.take<unsigned int>((size_t)h64.tiles);
+    }
+  }
   const int parts = kind == DELREC_SYNAPTIC ? 3 : 1;
   c.take<float>((size_t)pp.splits * N * N * parts);   // pair partials
   if (kind != DELREC_SYNAPTIC) {
@@ -795,6 +813,16 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
   int* boff = nullptr;
   const HybPlan hp = plan_hybrid_fast(ly, bp);
   const Hyb64Plan h64 = plan_hybrid64(ly, bp);
+  if (kind == DELREC_AXONAL && h64.ok) {
+    // offsets all 0: one bucket per source with all its synapses
+    offT = c.take<uint8_t>((size_t)N * N);
+    DR_CUDA(cudaMemsetAsync(offT, 0, (size_t)N * N, st));
+    ent = c.take<int2>((size_t)N * h64.CAP);
+    boff = c.take<int>((size_t)N * (h64.NKEY + 1));
+    const int nth = std::min(256, ((N + 31) / 32) * 32);
+    k_buckets<1><<<N, nth, (size_t)nth * 8, st>>>(N, h64.NKEY, h64.CAP, 8, W, offT, nullptr, s, ent, boff);
+    DR_LAUNCHED();
+  }
   if (kind != DELREC_AXONAL) {
     ent = c.take<int2>((size_t)N * bp.CAP);
     boff = c.take<int>((size_t)N * (bp.NKEY + 1));
@@ -819,10 +847,13 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
   if (kind == DELREC_HYBRID) {
     grx = c.take<float>((size_t)2 * cdiv(B, 64) * N * 64);
     arrive = c.take<unsigned int>((size_t)cdiv(B, 32));
+  } else if (kind == DELREC_AXONAL && h64.ok) {
+    grx = c.take<float>((size_t)2 * h64.tiles * N * 64);
+    arrive = c.take<unsigned int>((size_t)h64.tiles);
   }
   if (h64.ok) {
     Hyb64Args h{};
-    h.T = T; h.B = B; h.N = N; h.K = ly->K; h.CS = h64.CS; h.TAPS = bp.TAPS; h.CAPS = h64.CAPS; h.CAP = bp.CAP;
+    h.T = T; h.B = B; h.N = N; h.K = h64.K; h.CS = h64.CS; h.TAPS = bp.TAPS; h.CAPS = h64.CAPS; h.CAP = h64.CAP;
     h.gy = gy; h.u = u; h.keep = ly->has_keep ? keep : nullptr;
     h.tap_l0 = tl0; h.tap_nt = tnt; h.tap_w = tw; h.ent = ent; h.boff = boff;
     h.dx = g->dx; h.gr = gr; h.gz = gz; h.lif = a.lif;
