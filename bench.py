@@ -490,8 +490,8 @@ def roofline_probe(model, step, x, labels, spec, B):
     peaks, src = _peaks()
     peak = peaks["bf16_tflops_sustained"]
     achieved = flops / (ms / 1e3) / 1e12
-    per_unit = _profiled_traffic("k_bwd_hybrid") if spec["model"].endswith("hybrid_delays") else None
-    return {"bound": "tensor", "kernel": "k_bwd_hybrid (reverse scan of one recurrent layer)",
+    per_unit = _profiled_traffic("k_bwd_hybrid64") if spec["model"].endswith("hybrid_delays") else None
+    return {"bound": "tensor", "kernel": "k_bwd_hybrid64 (reverse scan of one recurrent layer)",
             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
             "traffic": per_unit * B * T if per_unit else None,
             "ms_per_launch": ms, "launches_timed": n, "flops_per_launch": flops,
