@@ -521,10 +521,13 @@ static int launch_pairs(int mode, const PairArgs& a, const PairPlan& p, int N, c
   return launch_pairs_b<2, 16>(a, p, N, st);
 }
 
-struct SrcPlan { int splits; };
+struct SrcPlan { int splits, tsplit; };
 static SrcPlan plan_src(const delrec_layer* ly) {
   SrcPlan p;
-  p.splits = cdiv(ly->B, 8);   // one partial row per chunk of 8 samples
+  // one partial row per chunk of 8 samples and time chunk (time chunks: the fused pass
+  // of the axonal / hybrid layers, so that enough threads stream)
+  p.tsplit = ly->kind == DELREC_SYNAPTIC ? 1 : std::max(1, std::min(4, ly->T / 64));
+  p.splits = cdiv(ly->B, 8) * p.tsplit;
   return p;
 }
 
@@ -543,68 +546,85 @@ static int cublas_for_device(cublasHandle_t* out) {
   return DELREC_OK;
 }
 
-// bytes of the tensor-core dW path: bf16 splits of gr and of each z variant, K+1 P
-// matrices, the cuBLAS workspace
+static int cublas_on(cublasHandle_t* h, void* cws, cudaStream_t st);
+
+// bytes of the tensor-core dW path: bf16 splits of gr (with nk-1 zero time rows appended)
+// and of each z variant, K+1 P matrices, the cuBLAS workspace
 static size_t dense_dw_ws(const delrec_layer* ly, int nz, int nk) {
   const size_t TBN = (size_t)ly->T * ly->B * ly->N, nn = (size_t)ly->N * ly->N;
+  const size_t pad = (size_t)(nk - 1) * ly->B * ly->N;
   Carve c(nullptr, (size_t)-1);
-  c.take<__nv_bfloat16>(TBN * 2);
+  c.take<__nv_bfloat16>((TBN + pad) * 2);
   c.take<__nv_bfloat16>(TBN * 2 * nz);
   if (nk > 1) c.take<float>(nn * nk);
   c.take<unsigned char>(kCublasWs);
   return c.off;
 }
 
-// dW (N,N) from gr (T,B,N) and the z variants z + v*TBN, v = min(k, nz-1) for offset k
-static int dense_dw(const delrec_layer* ly, const float* gr, const float* z, int nz, int nk,
-                    const uint8_t* offT, float* dW, Carve& c, cudaStream_t st) {
+// Buffers of the tensor-core dW path (inside the caller's workspace).
+struct DenseBufs {
+  __nv_bfloat16* g16;   // gr pieces: hi [GR], lo [GR]; GR = T*B*N + (nk-1)*B*N (zero tail)
+  __nv_bfloat16* z16;   // z variant v: hi at v*2*T*B*N, lo T*B*N after it
+  float* P;             // (nk, N, N) per-offset products, or dW itself when nk == 1
+  void* cws;            // cuBLAS workspace
+  size_t GR;
+};
+static bool dense_carve(const delrec_layer* ly, int nz, int nk, float* dW, Carve& c, DenseBufs* d) {
+  const size_t TBN = (size_t)ly->T * ly->B * ly->N, nn = (size_t)ly->N * ly->N;
+  d->GR = TBN + (size_t)(nk - 1) * ly->B * ly->N;
+  d->g16 = c.take<__nv_bfloat16>(d->GR * 2);
+  d->z16 = c.take<__nv_bfloat16>(TBN * 2 * nz);
+  d->P = nk > 1 ? c.take<float>(nn * nk) : dW;
+  d->cws = c.take<unsigned char>(kCublasWs);
+  return c.ok;
+}
+
+// dW (N,N) from gr (T,B,N) and the z variants (already in d.z16), v = min(k, nz-1) for
+// offset k.  P_k = sum_r Z_v(k)[r] (x) G[r + k*B] over the T*B rows r; the gr pieces carry
+// (nk-1)*B zero rows at the end, so every offset reads T*B rows and the offsets sharing
+// a z variant form one strided-batched GEMM (batch stride k*B*N on G, N*N on P).
+static int dense_dw(const delrec_layer* ly, const float* gr, int nz, int nk, const uint8_t* offT, float* dW,
+                    const DenseBufs& d, cudaStream_t st) {
   const int N = ly->N, T = ly->T, B = ly->B;
   const size_t TBN = (size_t)T * B * N, nn = (size_t)N * N;
-  __nv_bfloat16* g16 = c.take<__nv_bfloat16>(TBN * 2);
-  __nv_bfloat16* z16 = c.take<__nv_bfloat16>(TBN * 2 * nz);
-  float* P = nk > 1 ? c.take<float>(nn * nk) : dW;
-  void* cws = c.take<unsigned char>(kCublasWs);
-  if (!c.ok) return DELREC_ERR_WORKSPACE;
-  k_split_bf16<<<grid_for(TBN, 256), 256, 0, st>>>(gr, TBN, g16, g16 + TBN);
+  const size_t GR = d.GR;
+  k_split_bf16<<<grid_for(TBN, 256), 256, 0, st>>>(gr, TBN, d.g16, d.g16 + GR);
   DR_LAUNCHED();
-  for (int v = 0; v < nz; ++v) {
-    k_split_bf16<<<grid_for(TBN, 256), 256, 0, st>>>(z + (size_t)v * TBN, TBN, z16 + (size_t)v * 2 * TBN,
-                                                     z16 + (size_t)v * 2 * TBN + TBN);
-    DR_LAUNCHED();
+  if (GR > TBN) {
+    DR_CUDA(cudaMemsetAsync(d.g16 + TBN, 0, (GR - TBN) * sizeof(__nv_bfloat16), st));
+    DR_CUDA(cudaMemsetAsync(d.g16 + GR + TBN, 0, (GR - TBN) * sizeof(__nv_bfloat16), st));
   }
   cublasHandle_t h;
-  int rc = cublas_for_device(&h);
+  int rc = cublas_on(&h, d.cws, st);
   if (rc) return rc;
-  if (cublasSetStream(h, st) != CUBLAS_STATUS_SUCCESS) return DELREC_ERR_CUDA;
-  if (cublasSetWorkspace(h, cws, kCublasWs) != CUBLAS_STATUS_SUCCESS) return DELREC_ERR_CUDA;
   const float one = 1.f, zero = 0.f;
-  for (int k = 0; k < nk; ++k) {
-    const int rows = (T - k) * B;
-    float* Pk = P + (size_t)k * nn;
-    if (rows <= 0) {
-      DR_CUDA(cudaMemsetAsync(Pk, 0, nn * sizeof(float), st));
-      continue;
-    }
-    const int v = k < nz - 1 ? k : nz - 1;
-    const __nv_bfloat16* Zh = z16 + (size_t)v * 2 * TBN;
+  const int rows = T * B;
+  // offsets k < nz-1 use z variant k alone; k >= nz-1 share variant nz-1 (one batch)
+  for (int k0 = 0; k0 < nk;) {
+    const int v = k0 < nz - 1 ? k0 : nz - 1;
+    const int count = k0 < nz - 1 ? 1 : nk - k0;
+    const __nv_bfloat16* Zh = d.z16 + (size_t)v * 2 * TBN;
     const __nv_bfloat16* Zl = Zh + TBN;
-    const __nv_bfloat16* Gh = g16 + (size_t)k * B * N;
-    const __nv_bfloat16* Gl = g16 + TBN + (size_t)k * B * N;
-    // column-major view: C'(o,i) = sum_r Z'(o,r) G'(i,r)  ->  row-major dW[i][o]
+    const __nv_bfloat16* Gh = d.g16 + (size_t)k0 * B * N;
+    const __nv_bfloat16* Gl = d.g16 + GR + (size_t)k0 * B * N;
+    float* Pk = d.P + (size_t)k0 * nn;
+    // column-major view: C'(o,i) = sum_r Z'(o,r) G'(i,r)  ->  row-major P_k[i][o]
     const __nv_bfloat16* As[3] = {Zh, Zh, Zl};
     const __nv_bfloat16* Bs[3] = {Gh, Gl, Gh};
     for (int p = 0; p < 3; ++p) {
-      cublasStatus_t e = cublasGemmEx(h, CUBLAS_OP_N, CUBLAS_OP_T, N, N, rows, &one, As[p], CUDA_R_16BF, N,
-                                      Bs[p], CUDA_R_16BF, N, p == 0 ? &zero : &one, Pk, CUDA_R_32F, N,
-                                      CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+      const cublasStatus_t e = cublasGemmStridedBatchedEx(
+          h, CUBLAS_OP_N, CUBLAS_OP_T, N, N, rows, &one, As[p], CUDA_R_16BF, N, 0, Bs[p], CUDA_R_16BF, N,
+          (long long)B * N, p == 0 ? &zero : &one, Pk, CUDA_R_32F, N, (long long)nn, count, CUBLAS_COMPUTE_32F,
+          CUBLAS_GEMM_DEFAULT);
       if (e != CUBLAS_STATUS_SUCCESS) {
-        fprintf(stderr, "delrec_b200: cublasGemmEx failed (%d)\n", (int)e);
+        fprintf(stderr, "delrec_b200: cublasGemmStridedBatchedEx failed (%d)\n", (int)e);
         return DELREC_ERR_CUDA;
       }
     }
+    k0 += count;
   }
   if (nk > 1) {
-    k_pick_by_offset<<<grid_for(nn, 256), 256, 0, st>>>(N, offT, P, dW);
+    k_pick_by_offset<<<grid_for(nn, 256), 256, 0, st>>>(N, offT, d.P, dW);
     DR_LAUNCHED();
   }
   return DELREC_OK;
@@ -733,7 +753,6 @@ static size_t backward_ws(const delrec_layer* ly, int kind) {
   c.take<float>(TBN);                                  // gr
   if (kind != DELREC_SYNAPTIC) {
     c.take<float>(TBN * (bp.MM + 1));                  // gz_m
-    c.take<float>(TBN * (bp.MM + 1));                  // z_m
     c.take<int>(N); c.take<int>(N); c.take<float>(N * bp.TAPS);
   }
   if (kind == DELREC_HYBRID) c.take<uint8_t>(N * N);   // offT
@@ -780,15 +799,16 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
   if (wsb < backward_ws(ly, kind)) return DELREC_ERR_WORKSPACE;
   const BwdPlan bp = plan_backward(ly, kind);
   if (!bp.ok || bp.MM > kMMMax) return DELREC_ERR_UNSUPPORTED;
+  // k_source_pass keeps each neuron's spike history in 128 bits
+  if (kind != DELREC_SYNAPTIC && ly->L - 1 + bp.MM > 127) return DELREC_ERR_UNSUPPORTED;
   const int N = ly->N, T = ly->T, B = ly->B;
   const size_t TBN = (size_t)T * B * N;
   Carve c(ws, wsb);
   float* gr = c.take<float>(TBN);
-  float *gz = nullptr, *z = nullptr, *tw = nullptr;
+  float *gz = nullptr, *tw = nullptr;
   int *tl0 = nullptr, *tnt = nullptr;
   if (kind != DELREC_SYNAPTIC) {
     gz = c.take<float>(TBN * (bp.MM + 1));
-    z = c.take<float>(TBN * (bp.MM + 1));
     tl0 = c.take<int>(N);
     tnt = c.take<int>(N);
     tw = c.take<float>((size_t)N * bp.TAPS);
@@ -879,34 +899,59 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
   float* dsm = kind == DELREC_SYNAPTIC ? c.take<float>((size_t)N * N) : nullptr;
   const SrcPlan sp = plan_src(ly);
   float* spart = c.take<float>((size_t)sp.splits * N * (bp.TAPS + 1));
+  // per-neuron sums: db (all kinds), dd/ds of the axonal / hybrid base
+  const bool need_src = g->dbias || (kind != DELREC_SYNAPTIC && (g->dd || g->ds));
+  SrcArgs sa{};
+  sa.T = T; sa.B = B; sa.N = N; sa.TAPS = bp.TAPS;
+  sa.gr = gr; sa.gz = kind != DELREC_SYNAPTIC ? gz : nullptr; sa.y = y; sa.tap_l0 = tl0; sa.tap_nt = tnt;
+  sa.tap_w = tw; sa.part = spart; sa.MM = bp.MM;
+  const dim3 sgrid(cdiv(N, 32), cdiv(B, 8), sp.tsplit);
   if (kind != DELREC_SYNAPTIC) {
-    k_axonal_z<<<grid_for(TBN, 256), 256, 0, st>>>(T, B, N, bp.TAPS, bp.MM + 1, y, tl0, tnt, tw, z);
-    DR_LAUNCHED();
-  }
-  if (g->dW && kind != DELREC_SYNAPTIC) {
-    // tensor-core path: K+1 shifted GEMMs and a per-synapse pick
-    const size_t dws = dense_dw_ws(ly, bp.MM + 1, kind == DELREC_HYBRID ? ly->K + 1 : 1);
-    unsigned char* region = c.take<unsigned char>(dws);
-    Carve dc(region, dws);
-    rc = dense_dw(ly, gr, z, bp.MM + 1, kind == DELREC_HYBRID ? ly->K + 1 : 1, offT, g->dW, dc, st);
-    if (rc) return rc;
-  } else if (g->dW || (kind == DELREC_SYNAPTIC && (g->dd || g->ds))) {
-    PairArgs pa{};
-    pa.T = T; pa.B = B; pa.N = N; pa.KR = pp.KR; pa.BCH = pp.BCH; pa.rows_per_split = pp.rows_per_split;
-    pa.gr = gr; pa.Y = kind == DELREC_SYNAPTIC ? y : z; pa.offT = offT; pa.dT = dT; pa.s = s; pa.W = W;
-    pa.Lm1 = ly->L - 1;
-    pa.NZ = pp.NZ;
-    const size_t nn = (size_t)N * N;
-    pa.out_dW = ppart;
-    pa.out_dd = kind == DELREC_SYNAPTIC ? ppart + (size_t)pp.splits * nn : nullptr;
-    pa.out_ds = kind == DELREC_SYNAPTIC ? ppart + (size_t)2 * pp.splits * nn : nullptr;
-    rc = launch_pairs(bp.mode, pa, pp, N, st);
-    if (rc) return rc;
+    // one pass over (gr, y, gz at spikes) -> db/dmask partials and the bf16 z pieces of
+    // the tensor-core dW (K+1 shifted GEMMs and a per-synapse pick)
+    const int nz = bp.MM + 1, nk = kind == DELREC_HYBRID ? ly->K + 1 : 1;
+    DenseBufs dbf{};
     if (g->dW) {
-      k_sum_splits<<<grid_for(nn, 256), 256, 0, st>>>(pa.out_dW, pp.splits, nn, g->dW);
+      const size_t dws = dense_dw_ws(ly, nz, nk);
+      unsigned char* region = c.take<unsigned char>(dws);
+      Carve dc(region, dws);
+      if (!dense_carve(ly, nz, nk, g->dW, dc, &dbf)) return DELREC_ERR_WORKSPACE;
+    }
+    if (g->dW || need_src) {
+      const int wz = g->dW ? 1 : 0, warm = ly->L - 1 + bp.MM;
+      if (bp.MM == 0) {
+        if (bp.TAPS <= 4) k_source_pass<4, 0><<<sgrid, 256, 0, st>>>(sa, wz, warm, dbf.z16);
+        else if (bp.TAPS <= 8) k_source_pass<8, 0><<<sgrid, 256, 0, st>>>(sa, wz, warm, dbf.z16);
+        else k_source_pass<16, 0><<<sgrid, 256, 0, st>>>(sa, wz, warm, dbf.z16);
+      } else {
+        if (bp.TAPS <= 4) k_source_pass<4, 3><<<sgrid, 256, 0, st>>>(sa, wz, warm, dbf.z16);
+        else if (bp.TAPS <= 8) k_source_pass<8, 3><<<sgrid, 256, 0, st>>>(sa, wz, warm, dbf.z16);
+        else k_source_pass<16, 3><<<sgrid, 256, 0, st>>>(sa, wz, warm, dbf.z16);
+      }
       DR_LAUNCHED();
     }
-    if (kind == DELREC_SYNAPTIC) {
+    if (g->dW) {
+      rc = dense_dw(ly, gr, nz, nk, offT, g->dW, dbf, st);
+      if (rc) return rc;
+    }
+  } else {
+    if (g->dW || g->dd || g->ds) {
+      // synaptic pair sums (per-synapse lags): dW, dd, ds
+      PairArgs pa{};
+      pa.T = T; pa.B = B; pa.N = N; pa.KR = pp.KR; pa.BCH = pp.BCH; pa.rows_per_split = pp.rows_per_split;
+      pa.gr = gr; pa.Y = y; pa.offT = offT; pa.dT = dT; pa.s = s; pa.W = W;
+      pa.Lm1 = ly->L - 1;
+      pa.NZ = pp.NZ;
+      const size_t nn = (size_t)N * N;
+      pa.out_dW = ppart;
+      pa.out_dd = ppart + (size_t)pp.splits * nn;
+      pa.out_ds = ppart + (size_t)2 * pp.splits * nn;
+      rc = launch_pairs(bp.mode, pa, pp, N, st);
+      if (rc) return rc;
+      if (g->dW) {
+        k_sum_splits<<<grid_for(nn, 256), 256, 0, st>>>(pa.out_dW, pp.splits, nn, g->dW);
+        DR_LAUNCHED();
+      }
       if (g->dd) {
         k_sum_splits<<<grid_for(nn, 256), 256, 0, st>>>(pa.out_dd, pp.splits, nn, g->dd);
         DR_LAUNCHED();
@@ -918,20 +963,14 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
         DR_LAUNCHED();
       }
     }
+    if (need_src) {
+      if (bp.TAPS <= 4) k_source_reduce<4><<<sgrid, 256, 0, st>>>(sa);
+      else if (bp.TAPS <= 8) k_source_reduce<8><<<sgrid, 256, 0, st>>>(sa);
+      else k_source_reduce<16><<<sgrid, 256, 0, st>>>(sa);
+      DR_LAUNCHED();
+    }
   }
-  // per-neuron sums: db (all kinds), dd/ds of the axonal / hybrid base
-  const bool need_src = g->dbias || (kind != DELREC_SYNAPTIC && (g->dd || g->ds));
   if (need_src) {
-    SrcArgs sa{};
-    sa.T = T; sa.B = B; sa.N = N; sa.TAPS = bp.TAPS;
-    sa.gr = gr; sa.gz = kind != DELREC_SYNAPTIC ? gz : nullptr; sa.y = y; sa.tap_l0 = tl0; sa.tap_nt = tnt;
-    sa.part = spart;
-    sa.MM = bp.MM;
-    dim3 grid(cdiv(N, 32), sp.splits);
-    if (bp.TAPS <= 4) k_source_reduce<4><<<grid, 256, 0, st>>>(sa);
-    else if (bp.TAPS <= 8) k_source_reduce<8><<<grid, 256, 0, st>>>(sa);
-    else k_source_reduce<16><<<grid, 256, 0, st>>>(sa);
-    DR_LAUNCHED();
     const bool src_dd = kind != DELREC_SYNAPTIC;
     k_source_finalize<<<cdiv(N, 128), 128, 0, st>>>(N, bp.TAPS, sp.splits, spart, d, s, tl0, tnt,
                                                      g->dbias, src_dd ? g->dd : nullptr,

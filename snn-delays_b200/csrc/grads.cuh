@@ -16,6 +16,8 @@
 //   triangle derivatives (recdel_base.py:337-342 + AxonalRecdelTriton.backward :421-435).
 #pragma once
 
+#include <cuda_bf16.h>
+
 #include "prep.cuh"
 
 namespace delrec {
@@ -190,6 +192,7 @@ struct SrcArgs {
   const float* y;
   const int* tap_l0;
   const int* tap_nt;
+  const float* tap_w;   // k_source_pass: the taps' weights (z pieces)
   float* part;
 };
 
@@ -249,6 +252,153 @@ __global__ void __launch_bounds__(256) k_source_reduce(SrcArgs a) {
   __syncthreads();
   if (w == 0 && n < N) {
     float* out = a.part + ((size_t)blockIdx.y * N + n) * (a.TAPS + 1);
+    for (int j = 0; j < a.TAPS; ++j) {
+      float v = 0.f;
+      for (int g = 0; g < 8; ++g) v += j < TAPSMAX ? sred[g][lane][j] : 0.f;
+      out[j] = v;
+    }
+    float v = 0.f;
+    for (int g = 0; g < 8; ++g) v += sred[g][lane][TAPSMAX];
+    out[a.TAPS] = v;
+  }
+}
+
+// One time-major pass per (sample, neuron) for the axonal / hybrid layers, fusing
+//   * the per-neuron sums: db partials (sum of gr) and the dmask partials
+//     dmask[n][j] = sum_{t,b} gz_m(t)[b,n] y[t - l_j, b, n]  (m = max(0, 1 - l_j)), and
+//   * the bf16 pieces (hi, lo) of the interpolated delayed spikes
+//     z_m[t,b,o] = sum_{j: l_j >= 1-m} w_o[j] y[t - l_j, b, o]  (the weight-gradient GEMM
+//     operand, variant m for synapses whose offset reaches base lags <= 0).
+// Block = 32 neurons (lanes) x 8 samples (warps); grid.y over chunks of 8 samples, grid.z
+// over time chunks (each first replays the preceding L-1+MM steps of spikes).  gr, y and
+// gz_m are streamed once, coalesced, four steps per batch of independent loads.  y holds
+// spikes (0/1): the thread keeps its own spike history as a 128-bit shift register (bit
+// p = spike at t_in - p), so every lagged spike is a bit test.  Outputs for time te trail
+// the input time t_in by MM steps (base lags down to 1-MM look ahead).
+// Requires L - 1 + MM <= 127 and MM <= MMX.
+// bits [p0, p0 + 32) of the 128-bit history (h1:h0); positions below 0 read as 0
+__device__ __forceinline__ uint32_t hist_window(uint64_t h0, uint64_t h1, int p0) {
+  if (p0 < 0) return (uint32_t)(h0 << (-p0));
+  if (p0 >= 64) return (uint32_t)(h1 >> (p0 - 64));
+  if (p0 == 0) return (uint32_t)h0;
+  return (uint32_t)((h0 >> p0) | (h1 << (64 - p0)));
+}
+template <int TAPSMAX, int MMX>
+__global__ void __launch_bounds__(256, 3) k_source_pass(SrcArgs a, int want_z, int warm, __nv_bfloat16* __restrict__ zh) {
+  __shared__ float sred[8][32][TAPSMAX + 1];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int n = blockIdx.x * 32 + lane;
+  const int b = blockIdx.y * 8 + w;
+  const int N = a.N, B = a.B, T = a.T, MM = a.MM;
+  const int tch = (T + gridDim.z - 1) / gridDim.z;
+  const int c0 = blockIdx.z * tch, c1 = min(T, c0 + tch);   // this block's output times
+  float dm[TAPSMAX], tw[TAPSMAX];
+  float sg = 0.f;
+#pragma unroll
+  for (int j = 0; j < TAPSMAX; ++j) dm[j] = 0.f;
+  int lo = 1, nt = 0;
+  if (n < N) {
+    lo = a.tap_l0[n];
+    nt = a.tap_nt[n];
+  }
+  // taps j < nt with lag l_j = lo + j; a tap needing offset threshold m_j = max(0, 1-l_j)
+  // above MM never contributes.  zmask[m]: taps counted in z variant m (l_j >= 1 - m)
+  uint32_t tmask = 0u, zmask[MMX + 1];
+#pragma unroll
+  for (int m = 0; m <= MMX; ++m) zmask[m] = 0u;
+#pragma unroll
+  for (int j = 0; j < TAPSMAX; ++j) {
+    const int l = lo + j;
+    tw[j] = (n < N && j < nt) ? a.tap_w[(size_t)n * a.TAPS + j] : 0.f;
+    if (j < nt && 1 - l <= MM) tmask |= 1u << j;
+#pragma unroll
+    for (int m = 0; m <= MMX; ++m)
+      if (j < nt && m <= MM && l >= 1 - m) zmask[m] |= 1u << j;
+  }
+  if (n < N && b < B && c0 < c1) {
+    const size_t step = (size_t)B * N;
+    const size_t TBN = (size_t)T * step;
+    const size_t base = (size_t)b * N + n;
+    uint64_t h0 = 0ull, h1 = 0ull;
+    // warm-up: spikes of the steps before the chunk (8 independent loads per batch)
+    const int w0 = max(0, c0 + MM - warm), w1 = min(T, c0 + MM);
+    for (int t0 = w0; t0 < w1; t0 += 8) {
+      float yw[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) yw[q] = t0 + q < w1 ? __ldcs(a.y + (size_t)(t0 + q) * step + base) : 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (t0 + q >= w1) break;
+        h1 = (h1 << 1) | (h0 >> 63);
+        h0 = (h0 << 1) | (yw[q] != 0.f ? 1ull : 0ull);
+      }
+    }
+    // outputs te in [c0, c1), inputs t_in = te + MM
+    constexpr int U = 4;
+    for (int t0 = c0; t0 < c1; t0 += U) {
+      float g[U], yv[U], gzv[U][MMX + 1];
+#pragma unroll
+      for (int q = 0; q < U; ++q) {
+        const int te = t0 + q, tin = te + MM;
+        g[q] = te < c1 ? __ldcs(a.gr + (size_t)te * step + base) : 0.f;
+        yv[q] = (te < c1 && tin < T) ? __ldcs(a.y + (size_t)tin * step + base) : 0.f;
+#pragma unroll
+        for (int m = 0; m <= MMX; ++m)
+          gzv[q][m] = (a.gz && m <= MM && te < c1) ? __ldcs(a.gz + (size_t)m * TBN + (size_t)te * step + base) : 0.f;
+      }
+#pragma unroll
+      for (int q = 0; q < U; ++q) {
+        const int te = t0 + q;
+        if (te >= c1) break;
+        sg += g[q];
+        h1 = (h1 << 1) | (h0 >> 63);
+        h0 = (h0 << 1) | (yv[q] != 0.f ? 1ull : 0ull);
+        // bit j: spike at te - l_j  (history bit l_j + MM); spikes before t=0 read as 0
+        const uint32_t bits = hist_window(h0, h1, lo + MM) & tmask;
+        const size_t idx = (size_t)te * step + base;
+        if (bits == 0u) {
+          if (want_z) {
+            const __nv_bfloat16 zero = __float2bfloat16_rn(0.f);
+            for (int m = 0; m <= MM; ++m) {
+              zh[(size_t)m * 2 * TBN + idx] = zero;
+              zh[(size_t)m * 2 * TBN + TBN + idx] = zero;
+            }
+          }
+          continue;
+        }
+        if (a.gz) {
+#pragma unroll
+          for (int j = 0; j < TAPSMAX; ++j) {
+            const int mj = lo + j < 1 ? 1 - lo - j : 0;
+            float gsel = gzv[q][0];
+#pragma unroll
+            for (int m = 1; m <= MMX; ++m) gsel = m == mj ? gzv[q][m] : gsel;
+            if ((bits >> j) & 1u) dm[j] = __fadd_rn(dm[j], gsel);
+          }
+        }
+        if (want_z) {
+#pragma unroll
+          for (int m = 0; m <= MMX; ++m) {
+            if (m > MM) break;
+            const uint32_t zb = bits & zmask[m];
+            float acc = 0.f;
+#pragma unroll
+            for (int j = 0; j < TAPSMAX; ++j)
+              if ((zb >> j) & 1u) acc = __fadd_rn(acc, tw[j]);
+            const __nv_bfloat16 h = __float2bfloat16_rn(acc);
+            zh[(size_t)m * 2 * TBN + idx] = h;
+            zh[(size_t)m * 2 * TBN + TBN + idx] = __float2bfloat16_rn(acc - __bfloat162float(h));
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < TAPSMAX; ++j) sred[w][lane][j] = dm[j];
+  sred[w][lane][TAPSMAX] = sg;
+  __syncthreads();
+  if (w == 0 && n < N) {
+    float* out = a.part + (((size_t)blockIdx.z * gridDim.y + blockIdx.y) * N + n) * (a.TAPS + 1);
     for (int j = 0; j < a.TAPS; ++j) {
       float v = 0.f;
       for (int g = 0; g < 8; ++g) v += j < TAPSMAX ? sred[g][lane][j] : 0.f;

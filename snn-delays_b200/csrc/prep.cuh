@@ -173,30 +173,4 @@ __global__ void k_buckets(int N, int NKEY, int CAP, int PADM, const float* __res
   if (threadIdx.x == 0) bo[NKEY] = cnt < CAP ? cnt : CAP;
 }
 
-// z_m[t,b,o] = sum_{j: l_j >= 1-m} w_o[j] * y[t - l_j, b, o], l_j = l0_o + j, m = 0..NZ-1
-// (axonal interpolation of the spikes; the variant m keeps the base lags a synapse
-// with integer offset >= m receives).  z_m is stored at z + m*T*B*N.
-__global__ void k_axonal_z(int T, int B, int N, int TAPS, int NZ, const float* __restrict__ y,
-                           const int* __restrict__ l0, const int* __restrict__ nt,
-                           const float* __restrict__ w, float* __restrict__ z) {
-  const size_t total = (size_t)T * B * N;
-  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
-    const int o = (int)(e % N);
-    const size_t tb = e / N;
-    const int t = (int)(tb / B);
-    const int lo = l0[o], n = nt[o];
-    for (int m = 0; m < NZ; ++m) {
-      float acc = 0.f;
-      for (int j = 0; j < n; ++j) {
-        const int l = lo + j;
-        if (l < 1 - m) continue;
-        const int tt = t - l;
-        if (tt >= 0 && tt < T && y[(size_t)((long long)e - (long long)l * B * N)] != 0.f)
-          acc = __fadd_rn(acc, w[(size_t)o * TAPS + j]);
-      }
-      z[(size_t)m * total + e] = acc;
-    }
-  }
-}
-
 }  // namespace delrec
