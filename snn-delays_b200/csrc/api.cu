@@ -381,7 +381,7 @@ static int launch_hyb_t(const HybArgs& a, const HybPlan& h, cudaStream_t st) {
 // K <= 8, N <= 512 (gr of a tile staged in shared memory), at most 8 taps per source.
 struct Hyb64Plan {
   bool ok;
-  int CS, tiles, CAPS, KMAX, K, NKEY, CAP;
+  int CS, NT, tiles, CAPS, KMAX, K, NKEY, CAP;
   size_t smem;
 };
 static constexpr int kH64Taps = 8;
@@ -394,8 +394,12 @@ static Hyb64Plan plan_hybrid64(const delrec_layer* ly, const BwdPlan& bp) {
   h.K = ly->kind == DELREC_HYBRID ? ly->K : 0;
   if (bp.MM != 0 || h.K > 8 || ly->N > 512 || bp.TAPS > kH64Taps) return h;
   if (ly->B <= 32) return h;   // a 32-sample tile wastes no lanes there
-  h.CS = cdiv(ly->N, kH64NT);
   h.tiles = cdiv(ly->B, kH64BT);
+  // sources per block: fill the SMs (every block stages all N rows of gr, so not fewer
+  // than 12 sources per block)
+  h.NT = std::max(12, cdiv(ly->N * h.tiles, kSMs));
+  if (h.NT > kH64NTMax) return h;
+  h.CS = cdiv(ly->N, h.NT);
   if (h.CS * h.tiles > kSMs) return h;
   // small axonal layers keep the generic cluster scan (a few 64-sample blocks run slower)
   if (ly->kind == DELREC_AXONAL && h.CS * h.tiles < 32) return h;
@@ -403,7 +407,7 @@ static Hyb64Plan plan_hybrid64(const delrec_layer* ly, const BwdPlan& bp) {
   h.NKEY = h.K + 1;
   h.CAP = ly->kind == DELREC_HYBRID ? bp.CAP : h.CAPS;
   h.KMAX = h.K <= 4 ? 6 : 10;
-  h.smem = hyb64_smem_plan(ly->N, h.CAPS, h.K, bp.TAPS, h.KMAX).total;
+  h.smem = hyb64_smem_plan(ly->N, h.NT, h.CAPS, h.K, bp.TAPS, h.KMAX).total;
   h.ok = h.smem <= kSmemLimit;
   return h;
 }
@@ -873,7 +877,8 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
   }
   if (h64.ok) {
     Hyb64Args h{};
-    h.T = T; h.B = B; h.N = N; h.K = h64.K; h.CS = h64.CS; h.TAPS = bp.TAPS; h.CAPS = h64.CAPS; h.CAP = h64.CAP;
+    h.T = T; h.B = B; h.N = N; h.K = h64.K; h.CS = h64.CS; h.NT = h64.NT; h.TAPS = bp.TAPS; h.CAPS = h64.CAPS;
+    h.CAP = h64.CAP;
     h.gy = gy; h.u = u; h.keep = ly->has_keep ? keep : nullptr;
     h.tap_l0 = tl0; h.tap_nt = tnt; h.tap_w = tw; h.ent = ent; h.boff = boff;
     h.dx = g->dx; h.gr = gr; h.gz = gz; h.lif = a.lif;

@@ -2,7 +2,7 @@
 // 64-sample tiles (two samples per lane) and the synapse sums moved off the step-to-step
 // critical path.
 //
-// Layout: a block owns 16 source neurons o (one per warp) and a tile of 64 samples;
+// Layout: a block owns NT <= 16 source neurons o (one per warp) and a tile of 64 samples;
 // the blocks of a tile together cover all N neurons and exchange gr(t) through L2.
 // gr(t) of the tile (all N targets x 64 samples) is staged in shared memory as rows
 // grc[i][0..63]; lane l handles samples 2l and 2l+1 (one 8-byte load per synapse).
@@ -31,7 +31,7 @@
 namespace delrec {
 
 struct Hyb64Args {
-  int T, B, N, K, CS, TAPS, CAPS, CAP;
+  int T, B, N, K, CS, NT, TAPS, CAPS, CAP;   // NT <= 16 sources per block (one per warp)
   const float* gy;
   const float* u;
   const float* keep;
@@ -49,21 +49,21 @@ struct Hyb64Args {
   long long spin_limit;   // polls before a wait gives up (sets ST_TIMEOUT)
 };
 
-constexpr int kH64NT = 16, kH64BT = 64, kH64Threads = 512;
+constexpr int kH64NTMax = 16, kH64BT = 64, kH64Threads = 512;
 
 struct Hyb64Smem {
   size_t grc, idx, w, boff, taps, ring, total;
   int ring_stride;        // floats per source: KMAX*64 + 2 (bank offset between sources)
 };
-__host__ __device__ inline Hyb64Smem hyb64_smem_plan(int N, int CAPS, int K, int TAPS, int KMAX) {
+__host__ __device__ inline Hyb64Smem hyb64_smem_plan(int N, int NT, int CAPS, int K, int TAPS, int KMAX) {
   Hyb64Smem p;
   p.ring_stride = KMAX * 64 + 2;
   p.grc = align256((size_t)N * 64 * 4);
-  p.idx = align256((size_t)kH64NT * CAPS * 2);
-  p.w = align256((size_t)kH64NT * CAPS * 4);
-  p.boff = align256((size_t)kH64NT * (K + 2) * 4 + kH64NT * 4);
-  p.taps = align256((size_t)kH64NT * (TAPS + 2) * 4);
-  p.ring = align256((size_t)kH64NT * p.ring_stride * 4);
+  p.idx = align256((size_t)NT * CAPS * 2);
+  p.w = align256((size_t)NT * CAPS * 4);
+  p.boff = align256((size_t)NT * (K + 2) * 4 + NT * 4);
+  p.taps = align256((size_t)NT * (TAPS + 2) * 4);
+  p.ring = align256((size_t)NT * p.ring_stride * 4);
   p.total = p.grc + p.idx + p.w + p.boff + p.taps + p.ring;
   return p;
 }
@@ -99,7 +99,8 @@ template <int KMAX, int TPF>
 __global__ void __launch_bounds__(512, 1) k_bwd_hybrid64(Hyb64Args a) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ int s_abort;
-  constexpr int NT = kH64NT, BT = kH64BT, NTH = kH64Threads, PPT = 2;
+  constexpr int BT = kH64BT, NTH = kH64Threads, PPT = 2;   // NT * 64 <= PPT * NTH
+  const int NT = a.NT;
   const int rank = (int)(blockIdx.x % a.CS), tile = (int)(blockIdx.x / a.CS);
   const int tiles = (int)(gridDim.x / a.CS);
   const int N = a.N, T = a.T, B = a.B, K = a.K, tid = threadIdx.x;
@@ -110,7 +111,7 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid64(Hyb64Args a) {
   const int nb = max(0, min(BT, B - b0));
   const size_t BN = (size_t)B * N;
 
-  const Hyb64Smem P = hyb64_smem_plan(N, a.CAPS, K, a.TAPS, KMAX);
+  const Hyb64Smem P = hyb64_smem_plan(N, NT, a.CAPS, K, a.TAPS, KMAX);
   const int RS = P.ring_stride;
   float* grc = (float*)smem;                                                   // [N][64]
   uint16_t* sidx = (uint16_t*)(smem + P.grc);                                  // [NT][CAPS]
@@ -154,7 +155,7 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid64(Hyb64Args a) {
 
   // ---- per-thread pairs p = tid + k*NTH: ol = p % NT, bl = p / NT
   int pol[PPT], pbl[PPT];
-  bool pok[PPT];
+  bool pin[PPT], pok[PPT];   // pair inside the block's slice x tile; and a real sample
   float lam[PPT], kp[PPT];
   float pf_gy[PPT], pf_u[PPT], pf_tap[PPT][TPF];
 #pragma unroll
@@ -162,7 +163,8 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid64(Hyb64Args a) {
     const int p = tid + k * NTH;
     pol[k] = p % NT;
     pbl[k] = p / NT;
-    pok[k] = pol[k] < nts && pbl[k] < nb;
+    pin[k] = pol[k] < nts && pbl[k] < BT;
+    pok[k] = pin[k] && pbl[k] < nb;
     lam[k] = 0.f;
     kp[k] = (pok[k] && a.keep) ? a.keep[(size_t)(b0 + pbl[k]) * N + o0 + pol[k]] : 1.f;
   }
@@ -215,7 +217,7 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid64(Hyb64Args a) {
 #pragma unroll
     for (int k = 0; k < PPT; ++k) {
       const int ol = pol[k], bl = pbl[k];
-      if (ol >= nts) continue;
+      if (!pin[k]) continue;
       float grv = 0.f;
       float* rrow = ring + (size_t)ol * RS + bl;
       if (pok[k]) {
