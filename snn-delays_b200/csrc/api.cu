@@ -412,6 +412,32 @@ static Hyb64Plan plan_hybrid64(const delrec_layer* ly, const BwdPlan& bp) {
   return h;
 }
 
+// Synaptic layers in the 64-sample-tile scan: bucket k holds the synapse taps at lag k+1
+// (weight W*h), one unit base tap at lag 1; lags up to 31 (ring of 32 slots).
+static constexpr int kSynKmax = 32;
+static Hyb64Plan plan_syn64(const delrec_layer* ly) {
+  Hyb64Plan h{};
+  h.ok = false;
+  if (ly->kind != DELREC_SYNAPTIC || ly->N > 512 || ly->B <= 32) return h;
+  h.K = ly->L - 2;
+  if (h.K < 0 || h.K + 2 > kSynKmax) return h;
+  const int maxtaps = (int)ceilf(2.f * ly->s_max) + 1;   // integer lags inside one triangle
+  h.CAPS = (ly->N * maxtaps + 7 * (h.K + 1) + 7) / 8 * 8;
+  h.NKEY = ly->L;
+  h.KMAX = kSynKmax;
+  h.tiles = cdiv(ly->B, kH64BT);
+  int fit = 0;
+  for (int nt = kH64NTMax; nt >= 1 && !fit; --nt)
+    if (hyb64_smem_plan(ly->N, nt, h.CAPS, h.K, 1, h.KMAX).total <= kSmemLimit) fit = nt;
+  h.NT = std::max(4, cdiv(ly->N * h.tiles, kSMs));
+  if (fit == 0 || h.NT > fit) return h;
+  h.CS = cdiv(ly->N, h.NT);
+  if (h.CS * h.tiles > kSMs) return h;
+  h.smem = hyb64_smem_plan(ly->N, h.NT, h.CAPS, h.K, 1, h.KMAX).total;
+  h.ok = true;
+  return h;
+}
+
 template <int KMAX>
 static int launch_hyb64_t(const Hyb64Args& a, const Hyb64Plan& h, cudaStream_t st) {
   auto kern = k_bwd_hybrid64<KMAX, kH64Taps>;
@@ -769,6 +795,14 @@ static size_t backward_ws(const delrec_layer* ly, int kind) {
     c.take<float>((size_t)2 * cdiv(ly->B, 64) * N * 64);   // gr exchange (cooperative modes)
     c.take<unsigned int>((size_t)cdiv(ly->B, 32));         // arrival counters
   }
+  if (kind == DELREC_SYNAPTIC) {
+    const Hyb64Plan s64 = plan_syn64(ly);
+    if (s64.ok) {
+      c.take<int>(N); c.take<int>(N); c.take<float>(N);   // unit taps
+      c.take<float>((size_t)2 * s64.tiles * N * 64);
+      c.take<unsigned int>((size_t)s64.tiles);
+    }
+  }
   if (kind == DELREC_AXONAL) {
     const Hyb64Plan h64 = plan_hybrid64(ly, bp);
     if (h64.ok) {
@@ -837,6 +871,7 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
   int* boff = nullptr;
   const HybPlan hp = plan_hybrid_fast(ly, bp);
   const Hyb64Plan h64 = plan_hybrid64(ly, bp);
+  const Hyb64Plan s64 = plan_syn64(ly);
   if (kind == DELREC_AXONAL && h64.ok) {
     // offsets all 0: one bucket per source with all its synapses
     offT = c.take<uint8_t>((size_t)N * N);
@@ -852,7 +887,7 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
     boff = c.take<int>((size_t)N * (bp.NKEY + 1));
     const int nth = std::min(256, ((N + 31) / 32) * 32);
     const size_t sm = (size_t)nth * 8;
-    const int padm = (hp.ok || h64.ok) ? 8 : bp.PADM;
+    const int padm = (hp.ok || h64.ok || s64.ok) ? 8 : bp.PADM;
     if (kind == DELREC_HYBRID)
       k_buckets<1><<<N, nth, sm, st>>>(N, bp.NKEY, bp.CAP, padm, W, offT, nullptr, s, ent, boff);
     else
@@ -874,11 +909,29 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
   } else if (kind == DELREC_AXONAL && h64.ok) {
     grx = c.take<float>((size_t)2 * h64.tiles * N * 64);
     arrive = c.take<unsigned int>((size_t)h64.tiles);
+  } else if (kind == DELREC_SYNAPTIC && s64.ok) {
+    grx = c.take<float>((size_t)2 * s64.tiles * N * 64);
+    arrive = c.take<unsigned int>((size_t)s64.tiles);
   }
-  if (h64.ok) {
+  if (kind == DELREC_SYNAPTIC && s64.ok) {
+    int* ul0 = c.take<int>(N);
+    int* unt = c.take<int>(N);
+    float* uw = c.take<float>(N);
+    k_unit_taps<<<cdiv(N, 256), 256, 0, st>>>(N, ul0, unt, uw);
+    DR_LAUNCHED();
+    Hyb64Args h{};
+    h.T = T; h.B = B; h.N = N; h.K = s64.K; h.CS = s64.CS; h.NT = s64.NT; h.TAPS = 1; h.CAPS = s64.CAPS;
+    h.CAP = bp.CAP;
+    h.gy = gy; h.u = u; h.keep = ly->has_keep ? keep : nullptr;
+    h.tap_l0 = ul0; h.tap_nt = unt; h.tap_w = uw;
+    h.ent = ent; h.boff = boff + 1; h.boff_stride = bp.NKEY + 1;   // key 0 (lag 0) is empty
+    h.dx = g->dx; h.gr = gr; h.gz = nullptr; h.lif = a.lif;
+    h.grx = grx; h.arrive = arrive; h.spin_limit = 1ll << 22;
+    rc = launch_hyb64_t<kSynKmax>(h, s64, st);
+  } else if (h64.ok) {
     Hyb64Args h{};
     h.T = T; h.B = B; h.N = N; h.K = h64.K; h.CS = h64.CS; h.NT = h64.NT; h.TAPS = bp.TAPS; h.CAPS = h64.CAPS;
-    h.CAP = h64.CAP;
+    h.CAP = h64.CAP; h.boff_stride = h64.K + 2;
     h.gy = gy; h.u = u; h.keep = ly->has_keep ? keep : nullptr;
     h.tap_l0 = tl0; h.tap_nt = tnt; h.tap_w = tw; h.ent = ent; h.boff = boff;
     h.dx = g->dx; h.gr = gr; h.gz = gz; h.lif = a.lif;

@@ -39,10 +39,12 @@ struct Hyb64Args {
   const int* tap_nt;
   const float* tap_w;
   const int2* ent;        // (N, CAP) bucket entries (i, weight bits), buckets padded to 8
-  const int* boff;        // (N, K+2)
+  const int* boff;        // bucket k of source o starts at boff[o*boff_stride + k], k <= K+1
+  int boff_stride;
   float* dx;
   float* gr;
-  float* gz;              // (T,B,N)
+  float* gz;              // (T,B,N), or null when nothing downstream reads it (then no tap
+                          // may sit at lag >= 3)
   LifK lif;
   float* grx;             // [2][tiles][N][64] exchange of gr(t)
   unsigned int* arrive;   // [tiles] arrival counters, zero at launch
@@ -128,7 +130,7 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid64(Hyb64Args a) {
     const int ol = e / a.CAPS, pos = e % a.CAPS;
     int2 en = make_int2(0, 0);
     if (ol < nts) {
-      const int tot = a.boff[(size_t)(o0 + ol) * (K + 2) + K + 1];
+      const int tot = a.boff[(size_t)(o0 + ol) * a.boff_stride + K + 1];
       if (pos < tot) en = a.ent[(size_t)(o0 + ol) * a.CAP + pos];
     }
     sidx[e] = (uint16_t)en.x;
@@ -136,7 +138,12 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid64(Hyb64Args a) {
   }
   for (int e = tid; e < NT * (K + 2); e += NTH) {
     const int ol = e / (K + 2);
-    sbo[e] = ol < nts ? a.boff[(size_t)(o0 + ol) * (K + 2) + e % (K + 2)] : 0;
+    int off = ol < nts ? a.boff[(size_t)(o0 + ol) * a.boff_stride + e % (K + 2)] : 0;
+    if (off > a.CAPS) {   // the resident row holds CAPS entries (8-aligned)
+      flag_status(ST_INDEX_RANGE);
+      off = a.CAPS;
+    }
+    sbo[e] = off;
   }
   for (int ol = tid; ol < NT; ol += NTH) {
     const bool ok = ol < nts;
@@ -184,7 +191,7 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid64(Hyb64Args a) {
 #pragma unroll
         for (int j = 0; j < TPF; ++j) {
           const int l = lo + j;
-          if (j < n && l >= 3 && t + l < T) pf_tap[k][j] = __ldcg(a.gz + idx + (size_t)l * BN);
+          if (j < n && l >= 3 && t + l < T && a.gz) pf_tap[k][j] = __ldcg(a.gz + idx + (size_t)l * BN);
         }
       }
     }
@@ -267,7 +274,7 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid64(Hyb64Args a) {
     }
     __syncthreads();
     // ===== F: gz(t+1) is complete
-    if (t + 1 < T) {
+    if (t + 1 < T && a.gz) {
 #pragma unroll
       for (int k = 0; k < PPT; ++k)
         if (pok[k]) {
@@ -324,7 +331,7 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid64(Hyb64Args a) {
   __syncthreads();
 #pragma unroll
   for (int k = 0; k < PPT; ++k)
-    if (pok[k]) a.gz[((size_t)b0 + pbl[k]) * N + o0 + pol[k]] = ring[(size_t)pol[k] * RS + pbl[k]];
+    if (pok[k] && a.gz) a.gz[((size_t)b0 + pbl[k]) * N + o0 + pol[k]] = ring[(size_t)pol[k] * RS + pbl[k]];
 }
 
 }  // namespace delrec

@@ -102,6 +102,16 @@ __global__ void k_taps(const float* __restrict__ d, const float* __restrict__ s,
   for (int j = 0; j < TAPS; ++j) w[(size_t)o * TAPS + j] = j < n ? tri_h(tr, lo + j) : 0.f;
 }
 
+// A single tap at lag 1 with weight 1 per neuron (synaptic layers in the hybrid scan:
+// gfut(t) = gz(t+1) with the per-synapse lags carried by the bucket keys)
+__global__ void k_unit_taps(int N, int* __restrict__ l0, int* __restrict__ nt, float* __restrict__ w) {
+  const int o = blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= N) return;
+  l0[o] = 1;
+  nt[o] = 1;
+  w[o] = 1.f;
+}
+
 // Dense triangle mask out[r*L + l] (build_mask / build_syn_mask)
 __global__ void k_build_mask(int R, int L, const float* __restrict__ d, const float* __restrict__ s,
                              int s_period, float* __restrict__ out) {
