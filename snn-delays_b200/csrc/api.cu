@@ -12,6 +12,7 @@
 #include "backward.cuh"
 #include "backward_hybrid.cuh"
 #include "backward_hybrid64.cuh"
+#include "backward_axonal_mma.cuh"
 #include "dense.cuh"
 #include "forward.cuh"
 #include "grads.cuh"
@@ -438,6 +439,42 @@ static Hyb64Plan plan_syn64(const delrec_layer* ly) {
   return h;
 }
 
+// Axonal layers with the per-step contraction on tensor cores (backward_axonal_mma.cuh):
+// the same one-wave tiling as the 64-sample scan, 16 sources per block.
+struct AxMmaPlan {
+  bool ok;
+  int CS, tiles;
+  size_t smem;
+};
+static AxMmaPlan plan_axmma(const delrec_layer* ly, const BwdPlan& bp) {
+  AxMmaPlan h{};
+  h.ok = false;
+  if (ly->kind != DELREC_AXONAL || bp.MM != 0 || ly->N % 4 != 0 || ly->N > 1024 || bp.TAPS > kH64Taps) return h;
+  if (ly->B <= 32) return h;
+  h.CS = cdiv(ly->N, kAxNT);
+  h.tiles = cdiv(ly->B, kAxBT);
+  if (h.CS * h.tiles > kSMs || h.CS * h.tiles < 32) return h;
+  h.smem = axmma_smem_plan(ly->N, bp.TAPS).total;
+  h.ok = h.smem <= kSmemLimit;
+  return h;
+}
+static int launch_axmma(const AxMmaArgs& a, const AxMmaPlan& h, cudaStream_t st) {
+  auto kern = k_bwd_axonal_mma<kH64Taps>;
+  int rc = set_smem(kern, h.smem);
+  if (rc) return rc;
+  int per_sm = 0;
+  DR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kAxThreads, h.smem));
+  if (per_sm < 1 || h.CS * h.tiles > per_sm * kSMs) return DELREC_ERR_UNSUPPORTED;
+  DR_CUDA(cudaMemsetAsync(a.arrive, 0, sizeof(unsigned int) * h.tiles, st));
+  AxMmaArgs ac = a;
+  void* args[] = {(void*)&ac};
+  scan_mark(0, st);
+  DR_CUDA(cudaLaunchCooperativeKernel((const void*)kern, dim3(h.CS * h.tiles), dim3(kAxThreads), args, h.smem, st));
+  scan_mark(1, st);
+  ++g_launches;
+  return DELREC_OK;
+}
+
 template <int KMAX>
 static int launch_hyb64_t(const Hyb64Args& a, const Hyb64Plan& h, cudaStream_t st) {
   auto kern = k_bwd_hybrid64<KMAX, kH64Taps>;
@@ -803,7 +840,11 @@ static size_t backward_ws(const delrec_layer* ly, int kind) {
       c.take<unsigned int>((size_t)s64.tiles);
     }
   }
-  if (kind == DELREC_AXONAL) {
+  if (kind == DELREC_AXONAL && plan_axmma(ly, bp).ok) {
+    const AxMmaPlan am = plan_axmma(ly, bp);
+    c.take<float>((size_t)2 * am.tiles * N * 64);
+    c.take<unsigned int>((size_t)am.tiles);
+  } else if (kind == DELREC_AXONAL) {
     const Hyb64Plan h64 = plan_hybrid64(ly, bp);
     if (h64.ok) {
       c.take<uint8_t>(N * N);                              // zero offsets
@@ -870,7 +911,9 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
   int2* ent = nullptr;
   int* boff = nullptr;
   const HybPlan hp = plan_hybrid_fast(ly, bp);
-  const Hyb64Plan h64 = plan_hybrid64(ly, bp);
+  const AxMmaPlan am = plan_axmma(ly, bp);
+  Hyb64Plan h64 = plan_hybrid64(ly, bp);
+  if (am.ok) h64.ok = false;   // the tensor-core scan takes the axonal layer
   const Hyb64Plan s64 = plan_syn64(ly);
   if (kind == DELREC_AXONAL && h64.ok) {
     // offsets all 0: one bucket per source with all its synapses
@@ -912,8 +955,19 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
   } else if (kind == DELREC_SYNAPTIC && s64.ok) {
     grx = c.take<float>((size_t)2 * s64.tiles * N * 64);
     arrive = c.take<unsigned int>((size_t)s64.tiles);
+  } else if (am.ok) {
+    grx = c.take<float>((size_t)2 * am.tiles * N * 64);
+    arrive = c.take<unsigned int>((size_t)am.tiles);
   }
-  if (kind == DELREC_SYNAPTIC && s64.ok) {
+  if (am.ok) {
+    AxMmaArgs h{};
+    h.T = T; h.B = B; h.N = N; h.CS = am.CS; h.TAPS = bp.TAPS;
+    h.gy = gy; h.u = u; h.keep = ly->has_keep ? keep : nullptr; h.W = W;
+    h.tap_l0 = tl0; h.tap_nt = tnt; h.tap_w = tw;
+    h.dx = g->dx; h.gr = gr; h.gz = gz; h.lif = a.lif;
+    h.grx = grx; h.arrive = arrive; h.spin_limit = 1ll << 22;
+    rc = launch_axmma(h, am, st);
+  } else if (kind == DELREC_SYNAPTIC && s64.ok) {
     int* ul0 = c.take<int>(N);
     int* unt = c.take<int>(N);
     float* uw = c.take<float>(N);
