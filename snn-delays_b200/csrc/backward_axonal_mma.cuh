@@ -6,8 +6,10 @@
 // axonal contraction has no per-synapse offset, so each step's
 //   gz(t+1)[o, b] = sum_i W[i, o] gr(t+1)[i, b]      (o in the block's 16 sources)
 // is one dense 16 x 64 x N product.  fp32 accuracy from bf16: every operand is split
-// exactly into hi + lo pieces (hi = bf16(x), lo = bf16(x - hi)) and the product is
-// hi.hi + hi.lo + lo.hi (the dropped lo.lo term is below 2^-16 relative).
+// into hi + lo pieces (hi = x rounded to bf16; lo = x - hi, exact in fp32, rounded to
+// bf16: |x - hi - lo| <= 2^-17 |x|) and the product is hi.hi + hi.lo + lo.hi
+// (the dropped lo.lo term is below 2^-16 relative).  The split is integer arithmetic:
+// float <-> bf16 conversions run at a quarter of the ALU rate.
 //   W^T slice: Wp[piece][source][target], resident for the whole scan
 //   gr(t):     Gp[piece][sample][target], restaged every step from the L2 exchange
 //              (the exchange is sample-major: one float4 of targets -> 4 + 4 bf16)
@@ -59,6 +61,15 @@ __host__ __device__ inline AxMmaSmem axmma_smem_plan(int N, int TAPS) {
   p.total = p.gp + p.wp + p.ring + p.cred + p.taps;
   return p;
 }
+
+// hi/lo bf16 bit patterns of x in the upper halves of the returned words
+__device__ __forceinline__ void split_bits(float x, uint32_t& hi, uint32_t& lo) {
+  hi = (__float_as_uint(x) + 0x8000u) & 0xffff0000u;   // nearest bf16 (ties away from zero)
+  const float r = __fsub_rn(x, __uint_as_float(hi));      // exact: hi/2 <= x <= 2 hi
+  lo = (__float_as_uint(r) + 0x8000u) & 0xffff0000u;
+}
+// two bf16 (upper halves of a, b) packed as {a, b}
+__device__ __forceinline__ uint32_t pack_hi16(uint32_t a, uint32_t b) { return __byte_perm(a, b, 0x7632); }
 
 __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                uint32_t b0, uint32_t b1) {
@@ -135,9 +146,10 @@ __global__ void __launch_bounds__(512, 1) k_bwd_axonal_mma(AxMmaArgs a) {
   for (int e = tid; e < NT * ldk; e += NTH) {
     const int ol = e / ldk, i = e % ldk;
     const float wv = (ol < nts && i < N) ? a.W[(size_t)i * N + o0 + ol] : 0.f;
-    const __nv_bfloat16 h = __float2bfloat16_rn(wv);
-    Wp[e] = h;
-    Wp[(size_t)NT * ldk + e] = __float2bfloat16_rn(wv - __bfloat162float(h));
+    uint32_t hb, lb;
+    split_bits(wv, hb, lb);
+    Wp[e] = __ushort_as_bfloat16((unsigned short)(hb >> 16));
+    Wp[(size_t)NT * ldk + e] = __ushort_as_bfloat16((unsigned short)(lb >> 16));
   }
   for (int e = tid; e < 2 * BT * ldk; e += NTH) Gp[e] = __float2bfloat16_rn(0.f);
   for (int ol = tid; ol < NT; ol += NTH) {
@@ -306,23 +318,19 @@ __global__ void __launch_bounds__(512, 1) k_bwd_axonal_mma(AxMmaArgs a) {
     if (s_abort) return;
     {
       const int n4 = N / 4;   // N % 4 == 0 (planner)
-      const float4* xs = (const float4*)xb;
-      for (int v = tid; v < BT * n4; v += NTH) {
-        const int smp = v / n4, i4 = (v % n4) * 4;
-        const float4 x = __ldcg(xs + v);
-        const float xv[4] = {x.x, x.y, x.z, x.w};
-        __nv_bfloat16 hi[4], lo[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          hi[q] = __float2bfloat16_rn(xv[q]);
-          lo[q] = __float2bfloat16_rn(xv[q] - __bfloat162float(hi[q]));
+      for (int smp = warp; smp < BT; smp += NTH / 32) {
+        const float4* xs = (const float4*)(xb + (size_t)smp * N);
+        __nv_bfloat16* dh = Gp + (size_t)smp * ldk;
+        for (int i4 = lane; i4 < n4; i4 += 32) {
+          const float4 x = __ldcg(xs + i4);
+          uint32_t h0, l0, h1, l1, h2, l2, h3, l3;
+          split_bits(x.x, h0, l0);
+          split_bits(x.y, h1, l1);
+          split_bits(x.z, h2, l2);
+          split_bits(x.w, h3, l3);
+          *(uint2*)(dh + 4 * i4) = make_uint2(pack_hi16(h0, h1), pack_hi16(h2, h3));
+          *(uint2*)(dh + (size_t)BT * ldk + 4 * i4) = make_uint2(pack_hi16(l0, l1), pack_hi16(l2, l3));
         }
-        __nv_bfloat16* dh = Gp + (size_t)smp * ldk + i4;
-        *(uint2*)dh = make_uint2((uint32_t)__bfloat16_as_ushort(hi[0]) | ((uint32_t)__bfloat16_as_ushort(hi[1]) << 16),
-                                 (uint32_t)__bfloat16_as_ushort(hi[2]) | ((uint32_t)__bfloat16_as_ushort(hi[3]) << 16));
-        *(uint2*)(dh + (size_t)BT * ldk) =
-            make_uint2((uint32_t)__bfloat16_as_ushort(lo[0]) | ((uint32_t)__bfloat16_as_ushort(lo[1]) << 16),
-                       (uint32_t)__bfloat16_as_ushort(lo[2]) | ((uint32_t)__bfloat16_as_ushort(lo[3]) << 16));
       }
     }
     __syncthreads();
