@@ -176,3 +176,29 @@ def test_hybrid_base_edges(edge):
     ties, clean = compare_scan(got["y"], got["u"], ref["y"], ref["u"])
     assert clean, f"{ties} near-ties"
     compare_grads(got, ref, ["dx", "dW", "dd", "dbias"])
+
+
+@pytest.mark.parametrize("hidden,B", [([16], 4), ([64], 64), ([512], 100)])
+def test_hybrid_at_offset_scale_zero_is_the_axonal_model(hidden, B):
+    """SNN_recurrent_hybrid_delays with hybrid_offset_scale 0 and SNN_axonal_recurrent_delays
+    built from the same seed give bit-identical spikes, loss and gradients on the GPU
+    (tests/test_hybrid_delay_invariance.py:59-78 of the reference, at the tensor level)."""
+    from delrec import networks as nw
+    from model_configs import mem_config
+    cfg = mem_config(hidden=hidden, bias=True, T=24, B=B)
+    cfg.hybrid_offset_scale = 0
+    torch.manual_seed(0)
+    h = nw.SNN_recurrent_hybrid_delays(cfg).to(DEV)
+    torch.manual_seed(0)
+    a = nw.SNN_axonal_recurrent_delays(cfg).to(DEV)
+    g = torch.Generator().manual_seed(7)
+    x = (torch.rand(24, B, cfg.input_size, generator=g) < 0.2).float().to(DEV)
+    outs = []
+    for m in (h, a):
+        out = m(x)
+        out.pow(2).mean().backward()
+        outs.append((out.detach(), {k: p.grad.detach().clone() for k, p in m.named_parameters()}))
+    assert torch.equal(outs[0][0], outs[1][0])
+    assert outs[0][1].keys() == outs[1][1].keys()
+    for k in outs[0][1]:
+        assert torch.equal(outs[0][1][k], outs[1][1][k]), k
