@@ -177,7 +177,9 @@ def dist_setup(n_gpus):
         rank = int(os.environ["RANK"])
         local = int(os.environ.get("LOCAL_RANK", rank))
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        os.environ.setdefault("NCCL_DEBUG", "WARN")   # keep stdout to the one JSON line
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
         return rank, ws, local
     return 0, 1, 0
 
