@@ -176,6 +176,7 @@ static size_t forward_ws(const delrec_layer* ly, int kind) {
   } else {
     c.take<uint8_t>(N * N);                         // offT
     c.take<int>(N); c.take<int>(N); c.take<float>(N * p.TAPS);   // base taps
+    c.take<int4>(N * N);                            // scatter records
   }
   if (kind != DELREC_AXONAL && !p.ring_smem) c.take<float>((size_t)ly->B * ly->L * N);
   return c.off;
@@ -237,6 +238,10 @@ static int run_forward(const delrec_layer* ly, int kind, const delrec_lif* lif, 
     k_taps<<<cdiv(N, 256), 256, 0, st>>>(d, s, N, ly->L - 1, p.TAPS, 1 - ly->K, l0, nt, w);
     DR_LAUNCHED();
     a.tap_l0 = l0; a.tap_nt = nt; a.tap_w = w;
+    int4* rec = c.take<int4>((size_t)N * N);
+    k_syn_records<<<grid_for((size_t)N * N, 256), 256, 0, st>>>(N, ly->L, offT, WT, l0, nt, w, p.TAPS, rec);
+    DR_LAUNCHED();
+    a.rec = rec;
   }
   if (!p.ring_smem) a.ring_g = c.take<float>((size_t)ly->B * ly->L * N);
   const bool hyb = kind == DELREC_HYBRID;

@@ -20,6 +20,7 @@ struct FwdArgs {
   int T, B, N, L, R, NW, TAPS;
   const float* x;
   const float* WT;        // W transposed: WT[o*N + i] = W[i,o]
+  const int4* rec;        // hybrid: per-synapse scatter records (k_syn_records)
   const float* bias;      // (N) or null
   const float* keep;      // (B,N) or null
   const float* s;         // (N) half-widths
@@ -218,23 +219,39 @@ __global__ void __launch_bounds__(512) k_fwd_synaptic(FwdArgs a) {
       for (int q = 0; q < IPT; ++q) {
         const int i = q * NTH + tid;
         if (i >= N) continue;
-        float w[EB], dv[EB];
-        int kv[EB];   // hybrid integer offsets (no float round trip: conversions are quarter-rate)
-#pragma unroll
-        for (int j = 0; j < EB; ++j) {
-          if (j < ne) {
-            const size_t off = (size_t)oo[j] * N + i;
-            w[j] = __ldg(a.WT + off);
-            if (HYB) kv[j] = a.offT[off];
-            else dv[j] = __ldg(a.dT + off);
-          }
-        }
         if (HYB) {
+          // 16-byte records, four in flight (the kernel runs two blocks per SM: 64 registers)
+          constexpr int RB = 4;
 #pragma unroll
-          for (int j = 0; j < EB; ++j) {
+          for (int j0 = 0; j0 < EB; j0 += RB) {   // static: the event ids stay in registers
+          if (j0 >= ne) break;
+          int4 rv[RB];
+#pragma unroll
+          for (int jj = 0; jj < RB; ++jj)
+            if (j0 + jj < ne) rv[jj] = __ldg(a.rec + (size_t)oo[j0 + jj] * N + i);
+#pragma unroll
+          for (int jj = 0; jj < RB; ++jj) {
+            const int j = j0 + jj;
             if (j >= ne) break;
+            const int4 r = rv[jj];
+            if (r.x != kRecGeneric) {
+              const float wq[3] = {__int_as_float(r.y), __int_as_float(r.z), __int_as_float(r.w)};
+#pragma unroll
+              for (int q2 = 0; q2 < 3; ++q2) {
+                if (wq[q2] != 0.f) {
+                  int sl = slot + r.x + q2;   // lag in [1, L-1]
+                  if (sl >= L) sl -= L;
+                  float* cell = ring + (size_t)sl * N + i;
+                  *cell = __fadd_rn(*cell, wq[q2]);
+                }
+              }
+              continue;
+            }
+            // a source with a wide window: every tap of the base, shifted by the offset
             const int o = oo[j];
-            const int lo = s_l0[o] + kv[j], n = s_nt[o];
+            const size_t off = (size_t)o * N + i;
+            const float wj = __ldg(a.WT + off);
+            const int lo = s_l0[o] + (int)a.offT[off], n = s_nt[o];
             const float* hw = s_tw + (size_t)o * a.TAPS;
             for (int q2 = 0; q2 < n; ++q2) {
               const float h = hw[q2];
@@ -244,10 +261,20 @@ __global__ void __launch_bounds__(512) k_fwd_synaptic(FwdArgs a) {
               int sl = slot + l;
               if (sl >= L) sl -= L;
               float* cell = ring + (size_t)sl * N + i;
-              *cell = __fadd_rn(*cell, __fmul_rn(w[j], h));
+              *cell = __fadd_rn(*cell, __fmul_rn(wj, h));
             }
           }
+          }
           continue;
+        }
+        float w[EB], dv[EB];
+#pragma unroll
+        for (int j = 0; j < EB; ++j) {
+          if (j < ne) {
+            const size_t off = (size_t)oo[j] * N + i;
+            w[j] = __ldg(a.WT + off);
+            dv[j] = __ldg(a.dT + off);
+          }
         }
 #pragma unroll
         for (int j = 0; j < EB; ++j) {

@@ -112,6 +112,48 @@ __global__ void k_unit_taps(int N, int* __restrict__ l0, int* __restrict__ nt, f
   w[o] = 1.f;
 }
 
+// Scatter records of a hybrid layer's forward, one per synapse (o-major, like WT): the
+// positive base taps of source o shifted by the synapse's integer offset k,
+//   rec = {lag of the first positive tap + k, fl(W h_0), fl(W h_1), fl(W h_2)},
+// with the taps that land below lag 1 zeroed (they never enter the ring).  Sources with
+// more than 3 positive taps get lag = INT_MIN: the forward walks their full window.
+constexpr int kRecGeneric = -2147483647 - 1;
+__global__ void k_syn_records(int N, int L, const uint8_t* __restrict__ offT, const float* __restrict__ WT,
+                              const int* __restrict__ l0, const int* __restrict__ nt,
+                              const float* __restrict__ tw, int TAPS, int4* __restrict__ rec) {
+  const size_t nn = (size_t)N * N;
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < nn; e += (size_t)gridDim.x * blockDim.x) {
+    const int o = (int)(e / N);
+    const float* h = tw + (size_t)o * TAPS;
+    const int n = nt[o];
+    int first = -1, cnt = 0;
+    for (int j = 0; j < n; ++j)
+      if (h[j] > 0.f) {
+        if (first < 0) first = j;
+        cnt = j - first + 1;
+      }
+    int4 r = make_int4(1, 0, 0, 0);
+    if (cnt > 3) {
+      r.x = kRecGeneric;
+    } else if (first >= 0) {
+      const int lag0 = l0[o] + first + (int)offT[e];
+      const float w = WT[e];
+      float ws[3];
+#pragma unroll
+      for (int q = 0; q < 3; ++q) {
+        const int l = lag0 + q;
+        ws[q] = (q < cnt && l >= 1) ? __fmul_rn(w, h[first + q]) : 0.f;
+        if (q < cnt && l > L - 1) {
+          flag_status(ST_LAG_RANGE);
+          ws[q] = 0.f;
+        }
+      }
+      r = make_int4(lag0, __float_as_int(ws[0]), __float_as_int(ws[1]), __float_as_int(ws[2]));
+    }
+    rec[e] = r;
+  }
+}
+
 // Dense triangle mask out[r*L + l] (build_mask / build_syn_mask)
 __global__ void k_build_mask(int R, int L, const float* __restrict__ d, const float* __restrict__ s,
                              int s_period, float* __restrict__ out) {
