@@ -173,6 +173,7 @@ static size_t forward_ws(const delrec_layer* ly, int kind) {
     c.take<int>(N); c.take<int>(N); c.take<float>(N * p.TAPS);
   } else if (kind == DELREC_SYNAPTIC) {
     c.take<float>(N * N);                           // dT
+    c.take<int4>(N * N);                            // scatter records
   } else {
     c.take<uint8_t>(N * N);                         // offT
     c.take<int>(N); c.take<int>(N); c.take<float>(N * p.TAPS);   // base taps
@@ -225,6 +226,10 @@ static int run_forward(const delrec_layer* ly, int kind, const delrec_lif* lif, 
     k_transpose<<<tg, tb, 0, st>>>(d, dT, N, N);
     DR_LAUNCHED();
     a.dT = dT;
+    int4* rec = c.take<int4>((size_t)N * N);
+    k_syn_records_syn<<<grid_for((size_t)N * N, 256), 256, 0, st>>>(N, ly->L, dT, s, WT, rec);
+    DR_LAUNCHED();
+    a.rec = rec;
   } else {
     uint8_t* offT = c.take<uint8_t>((size_t)N * N);
     k_offsets_u8T<<<tg, tb, 0, st>>>(offsets, offT, N, ly->K);

@@ -20,7 +20,7 @@ struct FwdArgs {
   int T, B, N, L, R, NW, TAPS;
   const float* x;
   const float* WT;        // W transposed: WT[o*N + i] = W[i,o]
-  const int4* rec;        // hybrid: per-synapse scatter records (k_syn_records)
+  const int4* rec;        // per-synapse scatter records (k_syn_records / k_syn_records_syn)
   const float* bias;      // (N) or null
   const float* keep;      // (B,N) or null
   const float* s;         // (N) half-widths
@@ -219,11 +219,10 @@ __global__ void __launch_bounds__(512) k_fwd_synaptic(FwdArgs a) {
       for (int q = 0; q < IPT; ++q) {
         const int i = q * NTH + tid;
         if (i >= N) continue;
-        if (HYB) {
-          // 16-byte records, four in flight (the kernel runs two blocks per SM: 64 registers)
-          constexpr int RB = 4;
+        // 16-byte records, four in flight (the kernel runs two blocks per SM: 64 registers)
+        constexpr int RB = 4;
 #pragma unroll
-          for (int j0 = 0; j0 < EB; j0 += RB) {   // static: the event ids stay in registers
+        for (int j0 = 0; j0 < EB; j0 += RB) {   // static: the event ids stay in registers
           if (j0 >= ne) break;
           int4 rv[RB];
 #pragma unroll
@@ -247,55 +246,41 @@ __global__ void __launch_bounds__(512) k_fwd_synaptic(FwdArgs a) {
               }
               continue;
             }
-            // a source with a wide window: every tap of the base, shifted by the offset
+            // a synapse with a wide window: walk it
             const int o = oo[j];
             const size_t off = (size_t)o * N + i;
             const float wj = __ldg(a.WT + off);
-            const int lo = s_l0[o] + (int)a.offT[off], n = s_nt[o];
-            const float* hw = s_tw + (size_t)o * a.TAPS;
-            for (int q2 = 0; q2 < n; ++q2) {
-              const float h = hw[q2];
-              const int l = lo + q2;
-              if (!(h > 0.f) || l < 1) continue;
-              if (l > L - 1) { flag_status(ST_LAG_RANGE); continue; }
-              int sl = slot + l;
-              if (sl >= L) sl -= L;
-              float* cell = ring + (size_t)sl * N + i;
-              *cell = __fadd_rn(*cell, __fmul_rn(wj, h));
-            }
-          }
-          }
-          continue;
-        }
-        float w[EB], dv[EB];
-#pragma unroll
-        for (int j = 0; j < EB; ++j) {
-          if (j < ne) {
-            const size_t off = (size_t)oo[j] * N + i;
-            w[j] = __ldg(a.WT + off);
-            dv[j] = __ldg(a.dT + off);
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < EB; ++j) {
-          if (j >= ne) break;
-          const int o = oo[j];
-          const float d = dv[j];
-          const Tri tr = make_tri(d, s_s[o]);
-          int lo = (int)floorf(__fsub_rn(tr.onepd, tr.s));
-          int hi = (int)ceilf(__fadd_rn(tr.onepd, tr.s));
-          lo = lo < 1 ? 1 : lo;
-          if (hi > L - 1) {
-            if (tri_clamped(tr, L) > 0.f) flag_status(ST_LAG_RANGE);
-            hi = L - 1;
-          }
-          for (int l = lo; l <= hi; ++l) {
-            const float c = tri_clamped(tr, l);
-            if (c > 0.f) {
-              int sl = slot + l;
-              if (sl >= L) sl -= L;
-              float* cell = ring + (size_t)sl * N + i;
-              *cell = __fadd_rn(*cell, __fmul_rn(w[j], __fdiv_rn(c, tr.s2)));
+            if (HYB) {   // every tap of the base, shifted by the offset
+              const int lo = s_l0[o] + (int)a.offT[off], n = s_nt[o];
+              const float* hw = s_tw + (size_t)o * a.TAPS;
+              for (int q2 = 0; q2 < n; ++q2) {
+                const float h = hw[q2];
+                const int l = lo + q2;
+                if (!(h > 0.f) || l < 1) continue;
+                if (l > L - 1) { flag_status(ST_LAG_RANGE); continue; }
+                int sl = slot + l;
+                if (sl >= L) sl -= L;
+                float* cell = ring + (size_t)sl * N + i;
+                *cell = __fadd_rn(*cell, __fmul_rn(wj, h));
+              }
+            } else {     // the synapse's own triangle
+              const Tri tr = make_tri(__ldg(a.dT + off), s_s[o]);
+              int lo = (int)floorf(__fsub_rn(tr.onepd, tr.s));
+              int hi = (int)ceilf(__fadd_rn(tr.onepd, tr.s));
+              lo = lo < 1 ? 1 : lo;
+              if (hi > L - 1) {
+                if (tri_clamped(tr, L) > 0.f) flag_status(ST_LAG_RANGE);
+                hi = L - 1;
+              }
+              for (int l = lo; l <= hi; ++l) {
+                const float c = tri_clamped(tr, l);
+                if (c > 0.f) {
+                  int sl = slot + l;
+                  if (sl >= L) sl -= L;
+                  float* cell = ring + (size_t)sl * N + i;
+                  *cell = __fadd_rn(*cell, __fmul_rn(wj, __fdiv_rn(c, tr.s2)));
+                }
+              }
             }
           }
         }

@@ -154,6 +154,45 @@ __global__ void k_syn_records(int N, int L, const uint8_t* __restrict__ offT, co
   }
 }
 
+// Scatter records of a synaptic layer's forward (o-major): the positive lags of the
+// synapse's own triangle, rec = {first lag, fl(W fl(c_l / s^2)) for the next three lags}
+// (exactly the products the per-event loop forms), INT_MIN for wider triangles.
+__global__ void k_syn_records_syn(int N, int L, const float* __restrict__ dT, const float* __restrict__ s,
+                                  const float* __restrict__ WT, int4* __restrict__ rec) {
+  const size_t nn = (size_t)N * N;
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < nn; e += (size_t)gridDim.x * blockDim.x) {
+    const int o = (int)(e / N);
+    const Tri tr = make_tri(dT[e], s[o]);
+    int lo = (int)floorf(__fsub_rn(tr.onepd, tr.s));
+    int hi = (int)ceilf(__fadd_rn(tr.onepd, tr.s));
+    lo = lo < 1 ? 1 : lo;
+    if (hi > L - 1) {
+      if (tri_clamped(tr, L) > 0.f) flag_status(ST_LAG_RANGE);
+      hi = L - 1;
+    }
+    int first = -1, cnt = 0;
+    for (int l = lo; l <= hi; ++l)
+      if (tri_clamped(tr, l) > 0.f) {
+        if (first < 0) first = l;
+        cnt = l - first + 1;
+      }
+    int4 r = make_int4(1, 0, 0, 0);
+    if (cnt > 3) {
+      r.x = kRecGeneric;
+    } else if (first >= 0) {
+      const float w = WT[e];
+      float ws[3];
+#pragma unroll
+      for (int q = 0; q < 3; ++q) {
+        const float c = q < cnt ? tri_clamped(tr, first + q) : 0.f;
+        ws[q] = c > 0.f ? __fmul_rn(w, __fdiv_rn(c, tr.s2)) : 0.f;
+      }
+      r = make_int4(first, __float_as_int(ws[0]), __float_as_int(ws[1]), __float_as_int(ws[2]));
+    }
+    rec[e] = r;
+  }
+}
+
 // Dense triangle mask out[r*L + l] (build_mask / build_syn_mask)
 __global__ void k_build_mask(int R, int L, const float* __restrict__ d, const float* __restrict__ s,
                              int s_period, float* __restrict__ out) {
