@@ -176,27 +176,40 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid64(Hyb64Args a) {
     kp[k] = (pok[k] && a.keep) ? a.keep[(size_t)(b0 + pbl[k]) * N + o0 + pol[k]] : 1.f;
   }
   // loads for step t: gy, u and the taps l >= 3 (gz(t+l) was written at step t+l-1 >= t+2)
-  auto prefetch = [&](int t) {
+  // loads for step t: gy, u (issued at the start of step t+1) and the taps at lags >= 3
+  // with nonzero weight (issued after the deferred sums of step t+1: gz(t+l) was written at
+  // step t+l-1 >= t+2).  Split so that the load queue never holds a whole step's loads.
+  auto prefetch_lif = [&](int t) {
 #pragma unroll
     for (int k = 0; k < PPT; ++k) {
       pf_gy[k] = 0.f;
       pf_u[k] = 0.f;
-#pragma unroll
-      for (int j = 0; j < TPF; ++j) pf_tap[k][j] = 0.f;
       if (pok[k] && t >= 0) {
         const size_t idx = ((size_t)t * B + b0 + pbl[k]) * N + o0 + pol[k];
         pf_gy[k] = __ldcs(a.gy + idx);
         pf_u[k] = __ldcs(a.u + idx);
+      }
+    }
+  };
+  auto prefetch_taps = [&](int t) {
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+#pragma unroll
+      for (int j = 0; j < TPF; ++j) pf_tap[k][j] = 0.f;
+      if (pok[k] && t >= 0) {
+        const size_t idx = ((size_t)t * B + b0 + pbl[k]) * N + o0 + pol[k];
         const int lo = tl0[pol[k]], n = tnt[pol[k]];
 #pragma unroll
         for (int j = 0; j < TPF; ++j) {
           const int l = lo + j;
-          if (j < n && l >= 3 && t + l < T && a.gz) pf_tap[k][j] = __ldcg(a.gz + idx + (size_t)l * BN);
+          if (j < n && l >= 3 && t + l < T && a.gz && tw[pol[k] * a.TAPS + j] != 0.f)
+            pf_tap[k][j] = __ldcg(a.gz + idx + (size_t)l * BN);
         }
       }
     }
   };
-  prefetch(T - 1);
+  prefetch_lif(T - 1);
+  prefetch_taps(T - 1);
 
   const uint32_t gbase = (uint32_t)__cvta_generic_to_shared(grc) + lane * 8;
   const int ol_w = warp;   // the warp's source
@@ -218,7 +231,7 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid64(Hyb64Args a) {
 #pragma unroll
       for (int j = 0; j < TPF; ++j) cur_tap[k][j] = pf_tap[k][j];
     }
-    prefetch(t - 1);
+    prefetch_lif(t - 1);
     float* xb = a.grx + ((size_t)(t & 1) * tiles + tile) * xtile;
     // ===== A: LIF backward of the block's pairs
 #pragma unroll
@@ -251,8 +264,8 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid64(Hyb64Args a) {
       __stcg(xb + (size_t)(o0 + ol) * BT + bl, grv);
     }
     __syncthreads();
-    if (tid == 0) {
-      __threadfence();
+    if (tid == 0) {   // release: the block's exchange writes (ordered by the barrier) first
+      asm volatile("fence.acq_rel.gpu;" ::: "memory");
       atomicAdd(a.arrive + tile, 1u);
     }
     arrivals += a.CS;
@@ -282,6 +295,7 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid64(Hyb64Args a) {
           a.gz[idx] = ring[(size_t)pol[k] * RS + ((t + 1) % KMAX) * 64 + pbl[k]];
         }
     }
+    prefetch_taps(t - 1);
     // ===== W: the tile's gr(t)
     if (tid == 0) {
       long long polls = 0;
