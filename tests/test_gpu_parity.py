@@ -202,3 +202,36 @@ def test_hybrid_at_offset_scale_zero_is_the_axonal_model(hidden, B):
     assert outs[0][1].keys() == outs[1][1].keys()
     for k in outs[0][1]:
         assert torch.equal(outs[0][1][k], outs[1][1][k]), k
+
+
+def test_full_hybrid_model_matches_oracle_replay():
+    """The reference's test_hybrid_triton_matches_v2_on_gpu setup (MEM config, hidden 64,
+    T=24, B=8, offsets <= 4, loss out.pow(2).mean()), against the oracle replay of the same
+    network at the tighter tolerances: outputs 1e-5, gradients 1e-4 of each tensor's max."""
+    from delrec import networks as nw
+    from model_configs import mem_config
+    cfg = mem_config(hidden=[64], bias=False, T=24, B=8, C=8, K=4)
+    cfg.hybrid_offset_scale = 4
+    torch.manual_seed(0)
+    model = nw.SNN_recurrent_hybrid_delays(cfg).to(DEV)
+    g = torch.Generator().manual_seed(7)
+    x = (torch.rand(24, 8, cfg.input_size, generator=g) < 0.3).float() * 2.0
+    out = model(x.to(DEV))
+    out.pow(2).mean().backward()
+    lay = model.layers
+    rec = lay[2]
+    base = nw.learned_delay_parameter(rec, "recurrent_delays").detach().cpu().requires_grad_(True)
+    off = rec.parametrizations.recurrent_delays[0].offsets.cpu()
+    W = rec.recurrent_weights.detach().cpu().requires_grad_(True)
+    W0 = lay[0].weight.detach().cpu().requires_grad_(True)
+    W4 = lay[4].weight.detach().cpu().requires_grad_(True)
+    lif = O.OracleLIF(tau=2.0, v_threshold=1.0, v_reset=0.0, surrogate=O.ATanSpike(2.0))
+    y = O.synaptic_scan(x @ W0.t(), W, O.hybrid_delays(base, off), lif)
+    ref = y @ W4.t()
+    ref.pow(2).mean().backward()
+    assert rel_err(out.detach().cpu(), ref.detach()) < 1e-5
+    pairs = [(rec.recurrent_weights.grad, W.grad),
+             (nw.learned_delay_parameter(rec, "recurrent_delays").grad, base.grad),
+             (lay[0].weight.grad, W0.grad), (lay[4].weight.grad, W4.grad)]
+    for got, want in pairs:
+        assert rel_err(got.cpu(), want) < 1e-4

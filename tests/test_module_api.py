@@ -149,3 +149,38 @@ def test_feedforward_models_build():
     h = nw.SNN_hybrid_feedforward_delays(cfg)
     dc = [m for m in h.layers if isinstance(m, nw.dcls_module)][0]
     assert nw.learned_delay_parameter(dc, "P").shape[:3] == (1, 1, cfg.input_size)
+
+
+@pytest.mark.parametrize("hybrid_name,axonal_name", [
+    ("SNN_hybrid_feedforward_delays", "SNN_axonal_feedforward_delays"),
+    ("SNN_recurrent_hybrid_delays", "SNN_axonal_recurrent_delays"),
+])
+def test_maximum_positive_keeps_axonal_delay_budget(hybrid_name, axonal_name):
+    """tests/test_hybrid_delay_invariance.py:81-109 of the reference (construction part):
+    one learned delay per source, as many delay leaves as the axonal model, frozen
+    integer offsets in [0, 4] stored as buffers."""
+    nw = _nw()
+    from delrec.delay_layers import axonal_recdel
+
+    def leaves(model, name):
+        kind = nw.dcls_module if name == "P" else axonal_recdel
+        return [nw.learned_delay_parameter(m, name) for m in model.layers if isinstance(m, kind)]
+
+    cfg = mem_config(hidden=[16], bias=True, T=10, B=4, C=8, K=3)
+    cfg.kernel_count = 1
+    cfg.hybrid_offset_scale = 4
+    torch.manual_seed(0)
+    h = getattr(nw, hybrid_name)(cfg)
+    cfg0 = mem_config(hidden=[16], bias=True, T=10, B=4, C=8, K=3)
+    cfg0.kernel_count = 1
+    cfg0.hybrid_offset_scale = 0
+    torch.manual_seed(0)
+    a = getattr(nw, axonal_name)(cfg0)
+    for name in ("P", "recurrent_delays"):
+        hl, al = leaves(h, name), leaves(a, name)
+        assert len(hl) == len(al)
+        for x, y in zip(hl, al):
+            assert x.requires_grad and x.numel() == y.numel()
+    offsets = [b for n, b in h.named_buffers() if n.endswith(".offsets")]
+    assert offsets and all(not b.requires_grad for b in offsets)
+    assert all(int(b.max()) <= 4 and int(b.min()) >= 0 for b in offsets)
