@@ -46,6 +46,9 @@ CONFIGS = {
                                     model="SNN_synaptic_recurrent_delays", dmax=25.0, offsets=0, rate=0.05),
     "cfg5_psmnist_axonal_512": dict(hidden=[512], C=1, K=10, T=784, B=256, model="SNN_axonal_recurrent_delays",
                                     dmax=64.0, offsets=0, rate=None),
+    "cfg2_har_dcls_hybrid_128": dict(hidden=[128], C=9, K=6, T=128, B=64,
+                                     model="SNN_hybrid_recurrent_and_feedforward_delays", dmax=8.0, offsets=4,
+                                     rate=None, input="normal"),
 }
 
 
@@ -68,7 +71,9 @@ def make_config(spec, B):
 def make_inputs(spec, B, seed=1, device="cpu"):
     g = torch.Generator().manual_seed(seed)
     T, C = spec["T"], spec["C"]
-    if spec["rate"] is None:   # PS-MNIST-shaped: one channel of intensities, permuted in time
+    if spec.get("input") == "normal":   # HAR-shaped: real-valued N(0,1) input currents
+        x = torch.randn(T, B, C, generator=g)
+    elif spec["rate"] is None:   # PS-MNIST-shaped: one channel of intensities, permuted in time
         x = torch.rand(B, T, generator=g)[:, torch.randperm(T, generator=g)].t().unsqueeze(-1)
     else:
         rates = torch.rand(C, generator=g) * spec["rate"]
@@ -220,6 +225,16 @@ def cpu_step_fn(model, spec, cfg):
             b = m.bias.detach().cpu().clone().requires_grad_(True) if m.bias is not None else None
             layers.append(("lin", w, b))
             params += [w] + ([b] if b is not None else [])
+        elif isinstance(m, networks.dcls_module):
+            w = m.weight.detach().cpu().clone().requires_grad_(True)
+            b = m.bias.detach().cpu().clone().requires_grad_(True) if m.bias is not None else None
+            P = m.P.detach().cpu().clone()          # effective positions (offsets included)
+            S = m.SIG.detach().cpu().clone()
+            layers.append(("dcls", w, b, P, S, m.dilated_kernel_size[0], m.groups, m.left_padding))
+            params += [w] + ([b] if b is not None else [])
+        elif not isinstance(m, (torch.nn.Dropout, networks.spike_registrator)) and \
+                type(m).__name__ not in ("Dropout",) and not hasattr(m, "recurrent_weights"):
+            raise NotImplementedError(f"oracle replay: unsupported module {type(m).__name__}")
         elif hasattr(m, "recurrent_weights"):
             W = m.recurrent_weights.detach().cpu().clone().requires_grad_(True)
             leaf = networks.learned_delay_parameter(m, "recurrent_delays")
@@ -236,6 +251,9 @@ def cpu_step_fn(model, spec, cfg):
         for L in layers:
             if L[0] == "lin":
                 h = h @ L[1].t() + (L[2] if L[2] is not None else 0.0)
+            elif L[0] == "dcls":
+                _, w, b, P, S, K, groups, lpad = L
+                h = O.dcls_conv(h, w, P, S, K, groups, lpad, b)
             else:
                 _, W, base, off, axonal = L
                 lif = O.OracleLIF(tau=cfg.tau, v_threshold=cfg.v_threshold, v_reset=cfg.v_reset,
@@ -516,7 +534,10 @@ def roofline_probe(model, step, x, labels, spec, B):
     peak = peaks["bf16_tflops_sustained"]
     achieved = flops / (ms / 1e3) / 1e12
     per_unit = _profiled_traffic("k_bwd_hybrid64") if spec["model"].endswith("hybrid_delays") else None
-    return {"bound": "tensor", "kernel": "k_bwd_hybrid64 (reverse scan of one recurrent layer)",
+    kern = {"hybrid": "k_bwd_hybrid64", "synaptic": "k_bwd_hybrid64 (synaptic buckets)",
+            "axonal": "k_bwd_axonal_mma or k_bwd (by size)"}
+    kind = "hybrid" if "hybrid" in spec["model"] else ("synaptic" if "synaptic" in spec["model"] else "axonal")
+    return {"bound": "tensor", "kernel": f"{kern[kind]}: reverse scan of one recurrent layer",
             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
             "traffic": per_unit * B * T if per_unit else None,
             "ms_per_launch": ms, "launches_timed": n, "flops_per_launch": flops,
