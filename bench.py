@@ -348,6 +348,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--T", type=int, default=None, help="override T (profiling of small cases)")
     ap.add_argument("--B", type=int, default=None, help="override the per-GPU batch")
+    ap.add_argument("--hidden", type=int, default=None,
+                    help="override the width of every recurrent layer (BASELINE config 5 sweeps it)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     spec = dict(CONFIGS[args.config])
@@ -355,6 +357,8 @@ def main():
         spec["T"] = args.T
     if args.B:
         spec["B"] = args.B
+    if args.hidden:
+        spec["hidden"] = [args.hidden] * len(spec["hidden"])
 
     if args.impl == "reference":
         run_reference_arm(args, spec)

@@ -821,6 +821,51 @@ static int run_linear_backward(int M, int K, int N, const float* x, const float*
   return DELREC_OK;
 }
 
+// Axonal layers too wide for the single-wave scans run step by step: per reverse step one
+// LIF-backward kernel and one bf16 GEMM gz(t) = [hi hi lo](gr(t)) . [W_hi; W_lo; W_hi].
+static bool plan_axstep(const delrec_layer* ly, const BwdPlan& bp, bool single_wave_ok) {
+  return ly->kind == DELREC_AXONAL && !single_wave_ok && ly->N > 512 && bp.MM == 0;
+}
+static size_t axstep_ws(const delrec_layer* ly) {
+  const size_t N = ly->N, BN = (size_t)ly->B * N;
+  Carve c(nullptr, (size_t)-1);
+  c.take<float>(BN);                          // lam
+  c.take<__nv_bfloat16>(3 * N * N);           // [W_hi; W_lo; W_hi]
+  c.take<__nv_bfloat16>(3 * BN);              // [hi | hi | lo] of gr(t)
+  c.take<unsigned char>(kCublasWs);
+  return c.off;
+}
+static int run_axstep(const delrec_layer* ly, const delrec_lif* lif, const float* gy, const float* u,
+                      const float* keep, const float* W, const int* tl0, const int* tnt, const float* tw,
+                      int TAPS, float* gz, float* gr, float* dx, Carve& c, cudaStream_t st) {
+  const int N = ly->N, B = ly->B, T = ly->T;
+  const size_t BN = (size_t)B * N, nn = (size_t)N * N;
+  float* lam = c.take<float>(BN);
+  __nv_bfloat16* Wp = c.take<__nv_bfloat16>(3 * nn);
+  __nv_bfloat16* g3 = c.take<__nv_bfloat16>(3 * BN);
+  void* cws = c.take<unsigned char>(kCublasWs);
+  if (!c.ok) return DELREC_ERR_WORKSPACE;
+  DR_CUDA(cudaMemsetAsync(lam, 0, BN * sizeof(float), st));
+  k_split_bf16<<<grid_for(nn, 256), 256, 0, st>>>(W, nn, Wp, Wp + nn);
+  DR_LAUNCHED();
+  DR_CUDA(cudaMemcpyAsync(Wp + 2 * nn, Wp, nn * sizeof(__nv_bfloat16), cudaMemcpyDeviceToDevice, st));
+  cublasHandle_t h;
+  int rc = cublas_on(&h, cws, st);
+  if (rc) return rc;
+  const LifK lk = make_lif(*lif);
+  scan_mark(0, st);
+  for (int t = T - 1; t >= 0; --t) {
+    k_step_lif_bwd<<<grid_for(BN, 256), 256, 0, st>>>(t, T, B, N, TAPS, gy, u, keep, tl0, tnt, tw, gz, lam, dx,
+                                                      gr, g3, lk);
+    DR_LAUNCHED();
+    // column-major: gz(t)^T (N x B) = [W_hi; W_lo; W_hi]-view (N x 3N) . g3-view (3N x B)
+    rc = gemm_bf16(h, CUBLAS_OP_N, CUBLAS_OP_N, N, B, 3 * N, Wp, N, g3, 3 * N, 0.f, gz + (size_t)t * BN, N);
+    if (rc) return rc;
+  }
+  scan_mark(1, st);
+  return DELREC_OK;
+}
+
 static size_t backward_ws(const delrec_layer* ly, int kind) {
   const BwdPlan bp = plan_backward(ly, kind);
   const PairPlan pp = plan_pairs(ly, bp.mode, nullptr);
@@ -850,6 +895,7 @@ static size_t backward_ws(const delrec_layer* ly, int kind) {
       c.take<unsigned int>((size_t)s64.tiles);
     }
   }
+  if (plan_axstep(ly, bp, plan_axmma(ly, bp).ok || plan_hybrid64(ly, bp).ok)) c.take<unsigned char>(axstep_ws(ly));
   if (kind == DELREC_AXONAL && plan_axmma(ly, bp).ok) {
     const AxMmaPlan am = plan_axmma(ly, bp);
     c.take<float>((size_t)2 * am.tiles * N * 64);
@@ -924,6 +970,7 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
   const AxMmaPlan am = plan_axmma(ly, bp);
   Hyb64Plan h64 = plan_hybrid64(ly, bp);
   if (am.ok) h64.ok = false;   // the tensor-core scan takes the axonal layer
+  const bool axstep = plan_axstep(ly, bp, am.ok || h64.ok);
   const Hyb64Plan s64 = plan_syn64(ly);
   if (kind == DELREC_AXONAL && h64.ok) {
     // offsets all 0: one bucket per source with all its synapses
@@ -969,7 +1016,12 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
     grx = c.take<float>((size_t)2 * am.tiles * N * 64);
     arrive = c.take<unsigned int>((size_t)am.tiles);
   }
-  if (am.ok) {
+  if (axstep) {
+    const size_t sws = axstep_ws(ly);
+    unsigned char* region = c.take<unsigned char>(sws);
+    Carve sc(region, sws);
+    rc = run_axstep(ly, lif, gy, u, ly->has_keep ? keep : nullptr, W, tl0, tnt, tw, bp.TAPS, gz, gr, g->dx, sc, st);
+  } else if (am.ok) {
     AxMmaArgs h{};
     h.T = T; h.B = B; h.N = N; h.CS = am.CS; h.TAPS = bp.TAPS;
     h.gy = gy; h.u = u; h.keep = ly->has_keep ? keep : nullptr; h.W = W;

@@ -26,6 +26,43 @@ __global__ void k_split_bf16(const float* __restrict__ x, size_t n, __nv_bfloat1
   }
 }
 
+// One reverse step of an axonal layer run step by step (layers too wide for the
+// single-wave scans): for every (b, o),
+//   gfut = sum_j w_o[j] gz(t + l_j)[b, o]  (gz of later steps, from the per-step GEMMs),
+//   LIF backward with the carried lam, gr = du * keep,
+// writing dx(t), gr(t) and the bf16 pieces of gr(t) laid out as the GEMM operand row
+// [hi | hi | lo] (3N per sample) for gz(t) = [hi hi lo] . [W_hi; W_lo; W_hi].
+__global__ void k_step_lif_bwd(int t, int T, int B, int N, int TAPS, const float* __restrict__ gy,
+                               const float* __restrict__ u, const float* __restrict__ keep,
+                               const int* __restrict__ l0, const int* __restrict__ nt,
+                               const float* __restrict__ tw, const float* __restrict__ gz,
+                               float* __restrict__ lam, float* __restrict__ dx, float* __restrict__ gr,
+                               __nv_bfloat16* __restrict__ g3, LifK lif) {
+  const size_t BN = (size_t)B * N;
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < BN; e += (size_t)gridDim.x * blockDim.x) {
+    const int o = (int)(e % N), b = (int)(e / N);
+    const size_t idx = (size_t)t * BN + e;
+    const int lo = l0[o], n = nt[o];
+    float gfut = 0.f;
+    for (int j = 0; j < n; ++j) {
+      const int l = lo + j;
+      if (l >= 1 && t + l < T) gfut = fmaf(tw[(size_t)o * TAPS + j], gz[idx + (size_t)l * BN], gfut);
+    }
+    const float gY = __fadd_rn(gy[idx], gfut);
+    const float du = lif_backward(gY, u[idx], lam[e], lif);
+    lam[e] = lif_carry(du, lif);
+    const float g = keep ? __fmul_rn(du, keep[e]) : du;
+    dx[idx] = du;
+    gr[idx] = g;
+    const __nv_bfloat16 h = __float2bfloat16_rn(g);
+    const __nv_bfloat16 l = __float2bfloat16_rn(g - __bfloat162float(h));
+    __nv_bfloat16* row = g3 + (size_t)b * 3 * N;
+    row[o] = h;
+    row[N + o] = h;
+    row[2 * N + o] = l;
+  }
+}
+
 // dW[i*N + o] = P[k_io][i*N + o]
 __global__ void k_pick_by_offset(int N, const uint8_t* __restrict__ offT, const float* __restrict__ P,
                                  float* __restrict__ dW) {

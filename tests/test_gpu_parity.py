@@ -128,6 +128,8 @@ SHAPES = [
     # axonal reverse scan on the tensor cores (dense per-step contraction)
     ("axonal", 30, 100, 512, 0.0, False, True, True, 25.0, 0),
     ("axonal", 20, 70, 384, 1.0, True, False, False, 10.0, 0),
+    # wide axonal layer: step-by-step reverse scan (per-step bf16 GEMM)
+    ("axonal", 20, 48, 768, 0.5, False, True, True, 20.0, 0),
     ("synaptic", 25, 100, 96, 1.0, True, False, False, 12.0, 0),
     ("hybrid", 30, 100, 200, 0.0, False, True, True, 20.0, 8),
     ("hybrid", 24, 70, 512, 0.0, False, False, False, 3.0, 2),
