@@ -25,6 +25,7 @@ namespace delrec {
 static constexpr size_t kSmemLimit = 227 * 1024;  // opt-in dynamic shared memory per block
 static constexpr int kSMs = 148;
 static constexpr int kTapsMax = 16;               // widest axonal tap window supported
+static constexpr size_t kCublasWs = 32u << 20;     // cuBLAS workspace slice of a call
 
 static inline int pow2_at_least(int x) {
   int r = 1;
@@ -164,13 +165,56 @@ static int launch_fwd_syn(const FwdArgs& a, const FwdPlan& p, cudaStream_t st) {
   return DELREC_OK;
 }
 
-static size_t forward_ws(const delrec_layer* ly, int kind) {
+// Wide axonal layers (N > 512) run their forward step by step: one LIF kernel (which also
+// forms the next step's interpolated spikes as bf16 pieces) and one GEMM per step.
+static bool axstep_fwd(const delrec_layer* ly) { return ly->kind == DELREC_AXONAL && ly->N > 512; }
+static int cublas_on(cublasHandle_t* h, void* cws, cudaStream_t st);
+static int gemm_bf16(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k,
+                     const void* A, int lda, const void* B, int ldb, float beta, float* C, int ldc);
+static int gemm_f32_exact(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k,
+                          const float* A, int lda, const float* B, int ldb, float* C, int ldc);
+// Wide axonal layer, one kernel + one fp32 GEMM per step:
+//   k_step_lif_fwd: LIF at t from rec(t), then z(t+1) (B x N, fp32);
+//   rec(t+1) = z(t+1) . W^T on IEEE fp32 (no tensor-core accumulation, whose truncating
+//   fp32 adds over K = N sources drift beyond the 1e-5 membrane contract at N >= 768).
+static int run_axstep_fwd(const delrec_layer* ly, const FwdArgs& a, const float* W, Carve& c, cudaStream_t st) {
+  const int N = ly->N, B = ly->B, T = ly->T;
+  const size_t BN = (size_t)B * N;
+  float* rec = c.take<float>(BN);
+  float* v = c.take<float>(BN);
+  float* z = c.take<float>(BN);
+  void* cws = c.take<unsigned char>(kCublasWs);
+  if (!c.ok) return DELREC_ERR_WORKSPACE;
+  k_fill_f32<<<grid_for(BN, 256), 256, 0, st>>>(v, BN, a.lif.v0);
+  DR_LAUNCHED();
+  cublasHandle_t h;
+  int rc = cublas_on(&h, cws, st);
+  if (rc) return rc;
+  for (int t = 0; t < T; ++t) {
+    k_step_lif_fwd<<<grid_for(BN, 256), 256, 0, st>>>(t, T, B, N, a.TAPS, a.x, rec, a.bias, a.keep, a.tap_l0,
+                                                      a.tap_nt, a.tap_w, v, a.y, a.u, z, a.lif);
+    DR_LAUNCHED();
+    if (t + 1 < T) {
+      // column-major: rec (N x B) = W^T-view^T (N x N) . z (N x B); W[i*N + j] target i, source j
+      rc = gemm_f32_exact(h, CUBLAS_OP_T, CUBLAS_OP_N, N, B, N, W, N, z, N, rec, N);
+      if (rc) return rc;
+    }
+  }
+  return DELREC_OK;
+}
+
+static size_t forward_ws(const delrec_layer* ly, int kind, bool allow_step = true) {
   const FwdPlan p = plan_forward(ly, kind);
   const size_t N = ly->N;
   Carve c(nullptr, (size_t)-1);
   c.take<float>(N * N);                             // WT
   if (kind == DELREC_AXONAL) {
     c.take<int>(N); c.take<int>(N); c.take<float>(N * p.TAPS);
+    if (allow_step && axstep_fwd(ly)) {   // step-by-step forward of a wide layer
+      const size_t BN = (size_t)ly->B * N;
+      c.take<float>(BN); c.take<float>(BN); c.take<float>(BN);
+      c.take<unsigned char>(kCublasWs);
+    }
   } else if (kind == DELREC_SYNAPTIC) {
     c.take<float>(N * N);                           // dT
     c.take<int4>(N * N);                            // scatter records
@@ -186,7 +230,7 @@ static size_t forward_ws(const delrec_layer* ly, int kind) {
 static int run_forward(const delrec_layer* ly, int kind, const delrec_lif* lif, const float* x,
                        const float* W, const float* bias, const float* d, const float* offsets,
                        const float* s, const float* keep, float* y, float* u, void* ws,
-                       size_t wsb, cudaStream_t st) {
+                       size_t wsb, cudaStream_t st, bool allow_step = true) {
   int rc = check_layer(ly, kind);
   if (rc) return rc;
   if (!lif || !x || !W || !d || !s || !y || !u) return DELREC_ERR_ARG;
@@ -194,7 +238,7 @@ static int run_forward(const delrec_layer* ly, int kind, const delrec_lif* lif, 
   if (ly->has_bias && !bias) return DELREC_ERR_ARG;
   if (ly->has_keep && !keep) return DELREC_ERR_ARG;
   if (((uintptr_t)ws & 255) != 0) return DELREC_ERR_WORKSPACE;
-  if (wsb < forward_ws(ly, kind)) return DELREC_ERR_WORKSPACE;
+  if (wsb < forward_ws(ly, kind, allow_step)) return DELREC_ERR_WORKSPACE;
   const FwdPlan p = plan_forward(ly, kind);
   const int N = ly->N;
   Carve c(ws, wsb);
@@ -214,6 +258,7 @@ static int run_forward(const delrec_layer* ly, int kind, const delrec_lif* lif, 
     k_taps<<<cdiv(N, 256), 256, 0, st>>>(d, s, N, ly->L - 1, p.TAPS, 1, l0, nt, w);
     DR_LAUNCHED();
     a.tap_l0 = l0; a.tap_nt = nt; a.tap_w = w;
+    if (allow_step && axstep_fwd(ly)) return run_axstep_fwd(ly, a, W, c, st);
     switch (p.ipt) {
       case 1: return launch_fwd_axonal<1>(a, p, st);
       case 2: return launch_fwd_axonal<2>(a, p, st);
@@ -609,7 +654,6 @@ static SrcPlan plan_src(const delrec_layer* ly) {
 }
 
 // ---- tensor-core dW (dense.cuh) -------------------------------------------------
-static constexpr size_t kCublasWs = 32u << 20;
 static cublasHandle_t g_cublas[64] = {nullptr};
 
 static int cublas_for_device(cublasHandle_t* out) {
@@ -744,6 +788,18 @@ static int gemm_bf16(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t t
                                         &beta, C, CUDA_R_32F, ldc, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
   if (e != CUBLAS_STATUS_SUCCESS) {
     fprintf(stderr, "delrec_b200: cublasGemmEx failed (%d)\n", (int)e);
+    return DELREC_ERR_CUDA;
+  }
+  return DELREC_OK;
+}
+// fp32 GEMM with IEEE fp32 products and sums (PEDANTIC: no TF32, no bf16 emulation).
+static int gemm_f32_exact(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k,
+                          const float* A, int lda, const float* B, int ldb, float* C, int ldc) {
+  const float one = 1.f, zero = 0.f;
+  const cublasStatus_t e = cublasGemmEx(h, ta, tb, m, n, k, &one, A, CUDA_R_32F, lda, B, CUDA_R_32F, ldb, &zero,
+                                        C, CUDA_R_32F, ldc, CUBLAS_COMPUTE_32F_PEDANTIC, CUBLAS_GEMM_DEFAULT);
+  if (e != CUBLAS_STATUS_SUCCESS) {
+    fprintf(stderr, "delrec_b200: cublasGemmEx (fp32) failed (%d)\n", (int)e);
     return DELREC_ERR_CUDA;
   }
   return DELREC_OK;
@@ -1361,10 +1417,10 @@ int delrec_axonal_forward_noalloc(const delrec_layer* ly, const delrec_lif* lif,
                                   const float* W, const float* bias, const float* d, const float* s,
                                   const float* keep, float* y, float* u, void* stream) {
   if (!ly) return DELREC_ERR_ARG;
-  if (forward_ws(ly, DELREC_AXONAL) > kNoAllocScratchBytes) {
+  if (forward_ws(ly, DELREC_AXONAL, false) > kNoAllocScratchBytes) {
     fprintf(stderr, "delrec_b200: delrec_axonal_forward_noalloc needs %zu bytes of scratch for N=%d, "
                     "more than its fixed %zu-byte array; use delrec_axonal_forward with a workspace\n",
-            forward_ws(ly, DELREC_AXONAL), (int)ly->N, kNoAllocScratchBytes);
+            forward_ws(ly, DELREC_AXONAL, false), (int)ly->N, kNoAllocScratchBytes);
     return DELREC_ERR_WORKSPACE;
   }
   int dev = 0;
@@ -1376,8 +1432,9 @@ int delrec_axonal_forward_noalloc(const delrec_layer* ly, const delrec_lif* lif,
     DR_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
     g_noalloc_ptr[dev] = p;
   }
+  // the per-sample scan only: the step-by-step forward of wide layers needs more scratch
   return run_forward(ly, DELREC_AXONAL, lif, x, W, bias, d, nullptr, s, keep, y, u, g_noalloc_ptr[dev],
-                     kNoAllocScratchBytes, (cudaStream_t)stream);
+                     kNoAllocScratchBytes, (cudaStream_t)stream, false);
 }
 
 }  // extern "C"

@@ -126,6 +126,49 @@ __global__ void k_pack_wt(int N, int K, int Np, int Kp, const float* __restrict_
   }
 }
 
+// One forward step of an axonal layer run step by step (layers too wide for the
+// per-sample scan): for every (b, n),
+//   LIF update at t from rec(t) (the previous step's GEMM; 0 at t = 0),
+//   z(t+1)[b, n] = sum_j w_n[j] y(t+1 - l_j)[b, n]   (n as a source; l_j >= 1),
+// z (B x N, fp32) is the operand of rec(t+1) = z . W^T.
+__global__ void k_step_lif_fwd(int t, int T, int B, int N, int TAPS, const float* __restrict__ x,
+                               const float* __restrict__ rec, const float* __restrict__ bias,
+                               const float* __restrict__ keep, const int* __restrict__ l0,
+                               const int* __restrict__ nt, const float* __restrict__ tw, float* __restrict__ v,
+                               float* __restrict__ y, float* __restrict__ u, float* __restrict__ z, LifK lif) {
+  const size_t BN = (size_t)B * N;
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < BN; e += (size_t)gridDim.x * blockDim.x) {
+    const int n = (int)(e % N);
+    const size_t idx = (size_t)t * BN + e;
+    const float bs = bias ? bias[n] : 0.f;
+    const float kp = keep ? keep[e] : 1.f;
+    const float r = __fmul_rn(__fadd_rn(t > 0 ? rec[e] : 0.f, bs), kp);
+    const float av = __fadd_rn(x[idx], r);
+    const float uu = lif_charge(v[e], av, lif);
+    const bool sp = lif_fire(uu, lif);
+    v[e] = lif_reset(uu, sp, lif);
+    y[idx] = sp ? 1.f : 0.f;
+    u[idx] = uu;
+    if (t + 1 < T) {
+      const int lo = l0[n], cnt = nt[n];
+      float zz = 0.f;
+      for (int j = 0; j < cnt; ++j) {
+        const int l = lo + j;
+        const int ts = t + 1 - l;
+        if (l < 1 || ts < 0) continue;
+        const bool s = l == 1 ? sp : (y[(size_t)ts * BN + e] != 0.f);
+        if (s) zz = __fadd_rn(zz, tw[(size_t)n * TAPS + j]);
+      }
+      z[e] = zz;
+    }
+  }
+}
+
+__global__ void k_fill_f32(float* __restrict__ p, size_t n, float value) {
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x)
+    p[e] = value;
+}
+
 // dW[n*K + c] = D[n][c] + D[Np+n][c] + D[2Np+n][c];  dbias[n] = the same at c = K.
 // D is (3*Np, Kp) row-major (the column-major Kp x 3Np GEMM output).
 __global__ void k_linear_dw_reduce(int N, int K, int Np, int Kp, const float* __restrict__ D,
