@@ -156,6 +156,19 @@ static int launch_fwd_axonal(const FwdArgs& a, const FwdPlan& p, cudaStream_t st
   DR_LAUNCHED();
   return DELREC_OK;
 }
+// the 4-neurons-per-thread axonal forward: N % 4 == 0, N <= 1024, 16-byte aligned rows
+static bool fwd_axonal4_ok(const delrec_layer* ly, const FwdArgs& a) {
+  const auto al = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+  return ly->N % 4 == 0 && ly->N <= 1024 && al(a.x) && al(a.y) && al(a.u) && al(a.WT);
+}
+static int launch_fwd_axonal4(const FwdArgs& a, const FwdPlan& p, cudaStream_t st) {
+  int rc = set_smem(k_fwd_axonal4<16>, p.smem);
+  if (rc) return rc;
+  const int nth = ((a.N / 4 + 31) / 32) * 32;
+  k_fwd_axonal4<16><<<a.B, nth, p.smem, st>>>(a);
+  DR_LAUNCHED();
+  return DELREC_OK;
+}
 template <int IPT, bool HYB>
 static int launch_fwd_syn(const FwdArgs& a, const FwdPlan& p, cudaStream_t st) {
   int rc = set_smem(k_fwd_synaptic<IPT, HYB>, p.smem);
@@ -259,6 +272,7 @@ static int run_forward(const delrec_layer* ly, int kind, const delrec_lif* lif, 
     DR_LAUNCHED();
     a.tap_l0 = l0; a.tap_nt = nt; a.tap_w = w;
     if (allow_step && axstep_fwd(ly)) return run_axstep_fwd(ly, a, W, c, st);
+    if (fwd_axonal4_ok(ly, a)) return launch_fwd_axonal4(a, p, st);
     switch (p.ipt) {
       case 1: return launch_fwd_axonal<1>(a, p, st);
       case 2: return launch_fwd_axonal<2>(a, p, st);

@@ -43,9 +43,12 @@ struct AxMmaArgs {
 };
 
 constexpr int kAxNT = 16, kAxBT = 64, kAxThreads = 512, kAxKMAX = 4;
+// A block with at most kAxUrgMax urgent sources takes their product of gr(t) in fp32 on
+// the CUDA cores while restaging gr(t) (W columns of those sources kept in fp32).
+constexpr int kAxUrgMax = 4;
 
 struct AxMmaSmem {
-  size_t gp, wp, ring, cred, taps, total;
+  size_t gp, wp, ring, cred, taps, wu, total;
   int ldk;                // bf16 per row: N + 8 (4-word bank offset between rows)
   int ring_stride;
 };
@@ -58,7 +61,8 @@ __host__ __device__ inline AxMmaSmem axmma_smem_plan(int N, int TAPS) {
   p.ring = align256((size_t)kAxNT * p.ring_stride * 4);
   p.cred = align256((size_t)8 * 32 * 4 * 4);
   p.taps = align256((size_t)kAxNT * (TAPS + 3) * 4);
-  p.total = p.gp + p.wp + p.ring + p.cred + p.taps;
+  p.wu = align256((size_t)kAxUrgMax * N * 4 + 16 * 4);
+  p.total = p.gp + p.wp + p.ring + p.cred + p.taps + p.wu;
   return p;
 }
 
@@ -116,6 +120,63 @@ __device__ __forceinline__ void ax_mma_pass(const __nv_bfloat16* __restrict__ Gp
   for (int q = 0; q < 4; ++q) out[q] = acc0[q] + acc1[q];
 }
 
+// Restage of gr(t) (sample-major exchange rows of N = 128 MI floats) as bf16 hi/lo pieces:
+// warp w takes samples w + 16 j (j < 4), a lane float4 i4 = lane + 32 m of each row; all
+// 4 MI loads are issued before the first split.  With `fuse`, the urgent sources'
+//   gz(t)[u, b] = sum_i W[i, u] gr(t)[i, b]
+// is summed in fp32 from the same registers (lane partials, then a warp tree) into the
+// ring cell `slot` of each urgent source.
+template <int MI>
+__device__ __forceinline__ void ax_restage(const float* __restrict__ xb, int N, __nv_bfloat16* __restrict__ Gp,
+                                           int ldk, int warp, int lane, bool fuse, int nurg,
+                                           const float* __restrict__ wu, const int* __restrict__ ulist,
+                                           float* __restrict__ ring, int RS, int slot, int nb) {
+  constexpr int J = kAxBT / 16;
+  float4 xr[J][MI];
+#pragma unroll
+  for (int j = 0; j < J; ++j)
+#pragma unroll
+    for (int m = 0; m < MI; ++m) xr[j][m] = __ldcg((const float4*)(xb + (size_t)(warp + 16 * j) * N) + lane + 32 * m);
+#pragma unroll
+  for (int j = 0; j < J; ++j)
+#pragma unroll
+    for (int m = 0; m < MI; ++m) {
+      __nv_bfloat16* dh = Gp + (size_t)(warp + 16 * j) * ldk + 4 * (lane + 32 * m);
+      uint32_t h0, l0, h1, l1, h2, l2, h3, l3;
+      split_bits(xr[j][m].x, h0, l0);
+      split_bits(xr[j][m].y, h1, l1);
+      split_bits(xr[j][m].z, h2, l2);
+      split_bits(xr[j][m].w, h3, l3);
+      *(uint2*)dh = make_uint2(pack_hi16(h0, h1), pack_hi16(h2, h3));
+      *(uint2*)(dh + (size_t)kAxBT * ldk) = make_uint2(pack_hi16(l0, l1), pack_hi16(l2, l3));
+    }
+  if (!fuse) return;
+  for (int q = 0; q < nurg; ++q) {
+    const float4* w4 = (const float4*)(wu + (size_t)q * N);
+    float v[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) v[j] = 0.f;
+#pragma unroll
+    for (int m = 0; m < MI; ++m) {
+      const float4 w = w4[lane + 32 * m];
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        v[j] = fmaf(w.x, xr[j][m].x, v[j]);
+        v[j] = fmaf(w.y, xr[j][m].y, v[j]);
+        v[j] = fmaf(w.z, xr[j][m].z, v[j]);
+        v[j] = fmaf(w.w, xr[j][m].w, v[j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) v[j] += __shfl_xor_sync(0xffffffffu, v[j], off);
+      const int smp = warp + 16 * j;
+      if (lane == 0 && smp < nb) ring[(size_t)ulist[q] * RS + slot + smp] += v[j];
+    }
+  }
+}
+
 template <int TPF>
 __global__ void __launch_bounds__(512, 1) k_bwd_axonal_mma(AxMmaArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -141,6 +202,8 @@ __global__ void __launch_bounds__(512, 1) k_bwd_axonal_mma(AxMmaArgs a) {
   int* tnt = tl0 + NT;
   int* surg = tnt + NT;
   float* tw = (float*)(surg + NT);                                               // [16][TAPS]
+  float* wu = (float*)(smem + P.gp + P.wp + P.ring + P.cred + P.taps);          // [kAxUrgMax][N]
+  int* ulist = (int*)(wu + (size_t)kAxUrgMax * N);                               // [kAxUrgMax]
 
   // ---- init: W pieces of the block's sources, taps, ring, staged gr = 0
   for (int e = tid; e < NT * ldk; e += NTH) {
@@ -165,12 +228,22 @@ __global__ void __launch_bounds__(512, 1) k_bwd_axonal_mma(AxMmaArgs a) {
   for (int e = tid; e < NT * RS; e += NTH) ring[e] = 0.f;
   if (tid == 0) {
     s_abort = 0;
-    int any = 0;
-    for (int ol = 0; ol < nts; ++ol) any |= a.tap_l0[o0 + ol] <= 1;
-    s_any_urg = any;
+    int nu = 0;
+    for (int ol = 0; ol < nts; ++ol)
+      if (a.tap_l0[o0 + ol] <= 1) {
+        if (nu < kAxUrgMax) ulist[nu] = ol;
+        ++nu;
+      }
+    s_any_urg = nu;
   }
   __syncthreads();
-  const bool any_urg = s_any_urg != 0;
+  const int nurg = s_any_urg;
+  const bool any_urg = nurg != 0;
+  // fused urgent product: whole float4 rows per lane (N % 128 == 0) and few urgent sources
+  const bool fuse_urg = any_urg && nurg <= kAxUrgMax && (N & 127) == 0 && N <= 512;
+  if (fuse_urg)
+    for (int e = tid; e < nurg * N; e += NTH) wu[e] = a.W[(size_t)(e % N) * N + o0 + ulist[e / N]];
+  __syncthreads();
 
   // ---- per-thread (source, sample) pairs p = tid + k*NTH: ol = p % NT, bl = p / NT
   int pol[PPT], pbl[PPT];
@@ -330,7 +403,13 @@ __global__ void __launch_bounds__(512, 1) k_bwd_axonal_mma(AxMmaArgs a) {
     }
     __syncthreads();
     if (s_abort) return;
-    {
+    if ((N & 127) == 0 && N <= 512) {
+      const int MI = N >> 7;
+      if (MI == 1) ax_restage<1>(xb, N, Gp, ldk, warp, lane, fuse_urg, nurg, wu, ulist, ring, RS, (t % KMAX) * 64, nb);
+      else if (MI == 2) ax_restage<2>(xb, N, Gp, ldk, warp, lane, fuse_urg, nurg, wu, ulist, ring, RS, (t % KMAX) * 64, nb);
+      else if (MI == 3) ax_restage<3>(xb, N, Gp, ldk, warp, lane, fuse_urg, nurg, wu, ulist, ring, RS, (t % KMAX) * 64, nb);
+      else ax_restage<4>(xb, N, Gp, ldk, warp, lane, fuse_urg, nurg, wu, ulist, ring, RS, (t % KMAX) * 64, nb);
+    } else {
       const int n4 = N / 4;   // N % 4 == 0 (planner)
       for (int smp = warp; smp < BT; smp += NTH / 32) {
         const float4* xs = (const float4*)(xb + (size_t)smp * N);
@@ -348,8 +427,9 @@ __global__ void __launch_bounds__(512, 1) k_bwd_axonal_mma(AxMmaArgs a) {
       }
     }
     __syncthreads();
-    // ===== C2: product of gr(t) for the urgent sources -> slot t
-    if (any_urg) contract(t, true);
+    // ===== C2: product of gr(t) for the urgent sources -> slot t (tensor cores when the
+    // restage did not take it)
+    if (any_urg && !fuse_urg) contract(t, true);
     __syncthreads();
   }
   // ---- gz(0): its deferred product of gr(0) (staged)

@@ -42,7 +42,7 @@ struct FwdArgs {
 //   hist  R*NW u32 | l0 N int | nt N int | w N*TAPS f32 | ev_o N int | ev_z N f32
 // --------------------------------------------------------------------------------
 template <int IPT>
-__global__ void __launch_bounds__(512) k_fwd_axonal(FwdArgs a) {
+__global__ void __launch_bounds__(512, 2) k_fwd_axonal(FwdArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ int s_warp[33];
   const int N = a.N, T = a.T, B = a.B, NTH = blockDim.x, tid = threadIdx.x;
@@ -88,19 +88,36 @@ __global__ void __launch_bounds__(512) k_fwd_axonal(FwdArgs a) {
       nev += block_compact(z != 0.f, o, z, ev_o, ev_z, nev, s_warp);
     }
     // ---- rec_i = sum over events of W[i,o] * z_o
+    // The W rows of EV events are loaded together (the loads depend only on the
+    // compacted event list), then accumulated in event order.
+    constexpr int EV = IPT >= 8 ? 2 : 16 / IPT;
     float acc[IPT];
 #pragma unroll
     for (int q = 0; q < IPT; ++q) acc[q] = 0.f;
-#pragma unroll 4
-    for (int e = 0; e < nev; ++e) {
-      const int o = ev_o[e];
-      const float zv = ev_z[e];
-      const float* wrow = a.WT + (size_t)o * N;
+    for (int e0 = 0; e0 < nev; e0 += EV) {
+      const int cnt = min(EV, nev - e0);
+      float wv[EV][IPT], zv[EV];
 #pragma unroll
-      for (int q = 0; q < IPT; ++q) {
-        const int i = q * NTH + tid;
-        if (i < N) acc[q] = fmaf(__ldg(wrow + i), zv, acc[q]);
+      for (int k = 0; k < EV; ++k) {
+        zv[k] = 0.f;
+#pragma unroll
+        for (int q = 0; q < IPT; ++q) wv[k][q] = 0.f;
+        if (k < cnt) {
+          const float* wrow = a.WT + (size_t)ev_o[e0 + k] * N;
+          zv[k] = ev_z[e0 + k];
+#pragma unroll
+          for (int q = 0; q < IPT; ++q) {
+            const int i = q * NTH + tid;
+            if (i < N) wv[k][q] = __ldg(wrow + i);
+          }
+        }
       }
+#pragma unroll
+      for (int k = 0; k < EV; ++k)
+        if (k < cnt) {
+#pragma unroll
+          for (int q = 0; q < IPT; ++q) acc[q] = fmaf(wv[k][q], zv[k], acc[q]);
+        }
     }
     // ---- LIF, outputs, spike bits
     const size_t rowoff = ((size_t)t * B + b) * N;
@@ -121,6 +138,136 @@ __global__ void __launch_bounds__(512) k_fwd_axonal(FwdArgs a) {
       const int word = (q * NTH + (tid & ~31)) >> 5;
       if ((tid & 31) == 0 && word < a.NW) hist[(size_t)(t & (a.R - 1)) * a.NW + word] = m;
     }
+    __syncthreads();
+  }
+}
+
+// --------------------------------------------------------------------------------
+// axonal, 4 neurons per thread (N % 4 == 0, 16-byte aligned x / y / u / WT rows): the
+// same step as k_fwd_axonal with every event costing one 16-byte W load and four FMAs
+// per thread instead of one load and one FMA, so the per-event bookkeeping (event
+// read, address) is shared by four targets.  The events are compacted in ascending
+// source order and accumulated in that order, so the result equals k_fwd_axonal's
+// bit for bit.   dynamic smem: hist R*NW u32 | l0 N int | nt N int | w N*TAPS f32 | ev N int2
+// --------------------------------------------------------------------------------
+template <int EV>
+__global__ void __launch_bounds__(256) k_fwd_axonal4(FwdArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ int s_warp[8];
+  const int N = a.N, T = a.T, B = a.B, NTH = blockDim.x, tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5, nw = NTH >> 5;
+  const int b = blockIdx.x;
+  uint32_t* hist = (uint32_t*)smem;
+  int* sl0 = (int*)(hist + (size_t)a.R * a.NW);
+  int* snt = sl0 + N;
+  float* sw = (float*)(snt + N);
+  int2* ev = (int2*)(sw + (size_t)N * a.TAPS);
+
+  for (int e = tid; e < a.R * a.NW; e += NTH) hist[e] = 0u;
+  for (int o = tid; o < N; o += NTH) { sl0[o] = a.tap_l0[o]; snt[o] = a.tap_nt[o]; }
+  for (int e = tid; e < N * a.TAPS; e += NTH) sw[e] = a.tap_w[e];
+
+  const int i0 = 4 * tid;       // the thread's neurons i0 .. i0+3 (targets, and sources of the gather)
+  const bool act = i0 < N;
+  float v[4], kp[4], bs[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    v[q] = a.lif.v0;
+    kp[q] = (a.keep && act) ? a.keep[(size_t)b * N + i0 + q] : 1.f;
+    bs[q] = (a.bias && act) ? a.bias[i0 + q] : 0.f;
+  }
+  __syncthreads();
+
+  for (int t = 0; t < T; ++t) {
+    // ---- z gather of the thread's 4 sources
+    float z[4];
+    int c = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      z[q] = 0.f;
+      if (act) {
+        const int o = i0 + q;
+        const int lo = sl0[o], n = snt[o];
+        const uint32_t bit = 1u << (o & 31);
+        for (int j = 0; j < n; ++j) {
+          const int tt = t - lo - j;
+          if (tt >= 0 && (hist[(size_t)(tt & (a.R - 1)) * a.NW + (o >> 5)] & bit))
+            z[q] = __fadd_rn(z[q], sw[(size_t)o * a.TAPS + j]);
+        }
+        c += z[q] != 0.f;
+      }
+    }
+    // ---- compaction in ascending source order (block scan of the per-thread counts)
+    int inc = c;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, inc, off);
+      if (lane >= off) inc += n;
+    }
+    if (lane == 31) s_warp[warp] = inc;
+    __syncthreads();
+    int pos = inc - c, nev = 0;
+    for (int w2 = 0; w2 < nw; ++w2) {
+      const int cw = s_warp[w2];
+      if (w2 < warp) pos += cw;
+      nev += cw;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (z[q] != 0.f) ev[pos++] = make_int2(i0 + q, __float_as_int(z[q]));
+    __syncthreads();
+    // ---- rec_i = sum over events of W[i,o] z_o: the W rows of EV events loaded together
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int e0 = 0; e0 < nev; e0 += EV) {
+      const int cnt = min(EV, nev - e0);
+      float4 wv[EV];
+      float zv[EV];
+#pragma unroll
+      for (int k = 0; k < EV; ++k) {
+        zv[k] = 0.f;
+        wv[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (k < cnt) {
+          const int2 e = ev[e0 + k];
+          zv[k] = __int_as_float(e.y);
+          if (act) wv[k] = __ldg((const float4*)(a.WT + (size_t)e.x * N + i0));
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < EV; ++k)
+        if (k < cnt) {
+          acc.x = fmaf(wv[k].x, zv[k], acc.x);
+          acc.y = fmaf(wv[k].y, zv[k], acc.y);
+          acc.z = fmaf(wv[k].z, zv[k], acc.z);
+          acc.w = fmaf(wv[k].w, zv[k], acc.w);
+        }
+    }
+    // ---- LIF, outputs, spike bits (8 threads fill one 32-neuron history word)
+    unsigned nib = 0;
+    if (act) {
+      const size_t rowoff = ((size_t)t * B + b) * N + i0;
+      const float4 x4 = __ldcs((const float4*)(a.x + rowoff));
+      const float xa[4] = {x4.x, x4.y, x4.z, x4.w};
+      const float ra[4] = {acc.x, acc.y, acc.z, acc.w};
+      float ya[4], ua[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float rec = __fmul_rn(__fadd_rn(ra[q], bs[q]), kp[q]);
+        const float av = __fadd_rn(xa[q], rec);
+        const float uu = lif_charge(v[q], av, a.lif);
+        const bool sp = lif_fire(uu, a.lif);
+        v[q] = lif_reset(uu, sp, a.lif);
+        ya[q] = sp ? 1.f : 0.f;
+        ua[q] = uu;
+        nib |= (sp ? 1u : 0u) << q;
+      }
+      __stcs((float4*)(a.y + rowoff), make_float4(ya[0], ya[1], ya[2], ya[3]));
+      __stcs((float4*)(a.u + rowoff), make_float4(ua[0], ua[1], ua[2], ua[3]));
+    }
+    unsigned wd = nib << (4 * (lane & 7));
+    wd |= __shfl_xor_sync(0xffffffffu, wd, 1);
+    wd |= __shfl_xor_sync(0xffffffffu, wd, 2);
+    wd |= __shfl_xor_sync(0xffffffffu, wd, 4);
+    if ((lane & 7) == 0 && act) hist[(size_t)(t & (a.R - 1)) * a.NW + (i0 >> 5)] = wd;
     __syncthreads();
   }
 }
