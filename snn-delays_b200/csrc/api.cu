@@ -162,10 +162,10 @@ static bool fwd_axonal4_ok(const delrec_layer* ly, const FwdArgs& a) {
   return ly->N % 4 == 0 && ly->N <= 1024 && al(a.x) && al(a.y) && al(a.u) && al(a.WT);
 }
 static int launch_fwd_axonal4(const FwdArgs& a, const FwdPlan& p, cudaStream_t st) {
-  int rc = set_smem(k_fwd_axonal4<16>, p.smem);
+  int rc = set_smem(k_fwd_axonal4<32>, p.smem);
   if (rc) return rc;
   const int nth = ((a.N / 4 + 31) / 32) * 32;
-  k_fwd_axonal4<16><<<a.B, nth, p.smem, st>>>(a);
+  k_fwd_axonal4<32><<<a.B, nth, p.smem, st>>>(a);
   DR_LAUNCHED();
   return DELREC_OK;
 }

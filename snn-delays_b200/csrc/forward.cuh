@@ -176,9 +176,13 @@ __global__ void __launch_bounds__(256) k_fwd_axonal4(FwdArgs a) {
     kp[q] = (a.keep && act) ? a.keep[(size_t)b * N + i0 + q] : 1.f;
     bs[q] = (a.bias && act) ? a.bias[i0 + q] : 0.f;
   }
+  float4 xn = make_float4(0.f, 0.f, 0.f, 0.f);   // x of the next step, loaded a step ahead
+  if (act && T > 0) xn = __ldcs((const float4*)(a.x + (size_t)b * N + i0));
   __syncthreads();
 
   for (int t = 0; t < T; ++t) {
+    const float4 x4 = xn;
+    if (act && t + 1 < T) xn = __ldcs((const float4*)(a.x + ((size_t)(t + 1) * B + b) * N + i0));
     // ---- z gather of the thread's 4 sources
     float z[4];
     int c = 0;
@@ -245,7 +249,6 @@ __global__ void __launch_bounds__(256) k_fwd_axonal4(FwdArgs a) {
     unsigned nib = 0;
     if (act) {
       const size_t rowoff = ((size_t)t * B + b) * N + i0;
-      const float4 x4 = __ldcs((const float4*)(a.x + rowoff));
       const float xa[4] = {x4.x, x4.y, x4.z, x4.w};
       const float ra[4] = {acc.x, acc.y, acc.z, acc.w};
       float ya[4], ua[4];
