@@ -459,6 +459,10 @@ def main():
     #      steps, each bracketed by CUDA events on its own stream inside the library
     #      (every rank runs the steps: they contain the gradient all-reduce)
     roof = roofline_probe(model, step, x, labels, spec, B)
+    if roof is not None:
+        smem = scan_smem_roofline(model, spec, B, roof["ms_per_launch"], clk.summary().get("sm_mhz"))
+        if smem is not None:
+            roof["smem"] = smem
     step_roof = step_roofline(spec, B, ms)
 
     cpu = None
@@ -548,6 +552,31 @@ def roofline_probe(model, step, x, labels, spec, B):
             "peak_source": f"bf16_tflops_sustained ({src})",
             "traffic_source": "ncu dram bytes per sample-timestep of a T=50 capture, scaled to B*T"
                               if per_unit else None}
+
+
+SMEM_BYTES_PER_CLK_SM = 128   # shared-memory bandwidth per SM (32 banks x 4 bytes)
+N_SMS = 148
+
+
+def scan_smem_roofline(model, spec, B, ms, sm_mhz):
+    """Second roofline of the hybrid / synaptic reverse scan, whose per-step synapse sums
+    run on the CUDA cores from shared memory: every synapse reads its target's gr value
+    (4 bytes) once per sample-timestep, N^2*4*B*T algorithmic shared-memory bytes per
+    launch, against 128 bytes/clock/SM x 148 SMs at the median SM clock sampled during
+    the timed region (the record loads, the per-step restage and the ring traffic are
+    overhead on top)."""
+    if "hybrid" not in spec["model"] and "synaptic" not in spec["model"]:
+        return None
+    rec = [m for m in model.layers if hasattr(m, "recurrent_weights")]
+    if not rec or not sm_mhz or not ms:
+        return None
+    N = rec[0].neurons
+    nbytes = 4.0 * N * N * B * spec["T"]
+    achieved = nbytes / (ms / 1e3) / 1e12
+    peak = SMEM_BYTES_PER_CLK_SM * N_SMS * sm_mhz * 1e6 / 1e12
+    return {"bound": "smem", "achieved": achieved, "peak": peak, "unit": "TB/s", "frac": achieved / peak,
+            "bytes_per_launch": nbytes,
+            "peak_source": f"128 B/clk/SM x {N_SMS} SMs at the sampled median {sm_mhz:.0f} MHz"}
 
 
 def step_algorithmic(spec, B):
