@@ -605,56 +605,11 @@ static int launch_bwd_mode(const BwdArgs& a, const BwdPlan& p, cudaStream_t st) 
   }
 }
 
-// pair reduction planning
-struct PairPlan {
-  int KR, BCH, TW, splits, rows_per_split, NZ;
-  size_t smem;
-};
-static PairPlan plan_pairs(const delrec_layer* ly, int mode, const float* /*unused*/) {
-  PairPlan p;
-  p.NZ = mode == 1 ? hybrid_mm(ly) + 1 : 1;
-  const int N = ly->N;
-  int maxlag = 0;
-  if (mode == 1) maxlag = ly->K;
-  if (mode == 2) p.TW = std::min(std::max(std::min(ly->L - 1, 2 * (int)ceilf(ly->s_max) + 4), 1), 16);
-  else p.TW = 1;
-  if (mode == 2) maxlag = ly->L - 1 + 1;
-  p.KR = pow2_at_least(maxlag + p.TW + 1);
-  p.BCH = 32;
-  while (p.BCH > 8 && (size_t)(p.NZ * p.KR + 1) * p.BCH * 32 * 4 > 160 * 1024) p.BCH /= 2;
-  p.smem = (size_t)(p.NZ * p.KR + 1) * p.BCH * 32 * 4;
-  const int tiles = cdiv(N, 32) * cdiv(N, 32);
-  const int nbc = cdiv(ly->B, p.BCH);
-  int splits = std::max(1, std::min(nbc, cdiv(2 * kSMs, tiles)));
-  p.rows_per_split = cdiv(nbc, splits);
-  p.splits = cdiv(nbc, p.rows_per_split);
-  return p;
-}
-
-template <int MODE, int TW, int BCH>
-static int launch_pairs_t(const PairArgs& a, const PairPlan& p, int N, cudaStream_t st) {
-  auto kern = k_pair_reduce<MODE, TW, BCH>;
-  int rc = set_smem(kern, p.smem);
-  if (rc) return rc;
-  dim3 grid(cdiv(N, 32), cdiv(N, 32), p.splits);
-  kern<<<grid, 256, p.smem, st>>>(a);
-  DR_LAUNCHED();
-  return DELREC_OK;
-}
-template <int MODE, int TW>
-static int launch_pairs_b(const PairArgs& a, const PairPlan& p, int N, cudaStream_t st) {
-  switch (p.BCH) {
-    case 32: return launch_pairs_t<MODE, TW, 32>(a, p, N, st);
-    case 16: return launch_pairs_t<MODE, TW, 16>(a, p, N, st);
-    default: return launch_pairs_t<MODE, TW, 8>(a, p, N, st);
-  }
-}
-static int launch_pairs(int mode, const PairArgs& a, const PairPlan& p, int N, cudaStream_t st) {
-  if (mode == 0) return launch_pairs_b<0, 1>(a, p, N, st);
-  if (mode == 1) return launch_pairs_b<1, 1>(a, p, N, st);
-  if (p.TW <= 4) return launch_pairs_b<2, 4>(a, p, N, st);
-  if (p.TW <= 8) return launch_pairs_b<2, 8>(a, p, N, st);
-  return launch_pairs_b<2, 16>(a, p, N, st);
+// Synaptic weight-gradient lag window: the lags from max(1, floor(1 + d - s) - 1) that the
+// triangle (and its derivatives) of a synapse can touch, as a template width 4, 8 or 16.
+static int syn_window(const delrec_layer* ly) {
+  const int tw = std::min(std::max(std::min(ly->L - 1, 2 * (int)ceilf(ly->s_max) + 4), 1), 16);
+  return tw <= 4 ? 4 : (tw <= 8 ? 8 : 16);
 }
 
 struct SrcPlan { int splits, tsplit; };
@@ -761,6 +716,40 @@ static int dense_dw(const delrec_layer* ly, const float* gr, int nz, int nk, con
   if (nk > 1) {
     k_pick_by_offset<<<grid_for(nn, 256), 256, 0, st>>>(N, offT, d.P, dW);
     DR_LAUNCHED();
+  }
+  return DELREC_OK;
+}
+
+// Synaptic layers: the per-lag correlation stack C_l = sum_r G[r + l*B] (x) Y[r] for all
+// lags l = 0..L-1 (the reference's Cstack), as two strided-batched bf16 GEMMs over the
+// T*B rows: gr split into hi + lo pieces, the spikes exact in one piece.  d.P receives C.
+static int syn_cstack(const delrec_layer* ly, const float* gr, const float* y, const DenseBufs& d, cudaStream_t st) {
+  const int N = ly->N, T = ly->T, B = ly->B, nk = ly->L;
+  const size_t TBN = (size_t)T * B * N, nn = (size_t)N * N;
+  const size_t GR = d.GR;
+  k_split_bf16<<<grid_for(TBN, 256), 256, 0, st>>>(gr, TBN, d.g16, d.g16 + GR);
+  DR_LAUNCHED();
+  if (GR > TBN) {
+    DR_CUDA(cudaMemsetAsync(d.g16 + TBN, 0, (GR - TBN) * sizeof(__nv_bfloat16), st));
+    DR_CUDA(cudaMemsetAsync(d.g16 + GR + TBN, 0, (GR - TBN) * sizeof(__nv_bfloat16), st));
+  }
+  k_split_bf16<<<grid_for(TBN, 256), 256, 0, st>>>(y, TBN, d.z16, d.z16 + TBN);   // 0/1: lo = 0
+  DR_LAUNCHED();
+  cublasHandle_t h;
+  int rc = cublas_on(&h, d.cws, st);
+  if (rc) return rc;
+  const float one = 1.f, zero = 0.f;
+  const __nv_bfloat16* Gs[2] = {d.g16, d.g16 + GR};
+  for (int p = 0; p < 2; ++p) {
+    // column-major view: C'(o,i) = sum_r Y'(o,r) G'(i,r + l*B)  ->  row-major C_l[i][o]
+    const cublasStatus_t e = cublasGemmStridedBatchedEx(
+        h, CUBLAS_OP_N, CUBLAS_OP_T, N, N, T * B, &one, d.z16, CUDA_R_16BF, N, 0, Gs[p], CUDA_R_16BF, N,
+        (long long)B * N, p == 0 ? &zero : &one, d.P, CUDA_R_32F, N, (long long)nn, nk, CUBLAS_COMPUTE_32F,
+        CUBLAS_GEMM_DEFAULT);
+    if (e != CUBLAS_STATUS_SUCCESS) {
+      fprintf(stderr, "delrec_b200: cublasGemmStridedBatchedEx failed (%d)\n", (int)e);
+      return DELREC_ERR_CUDA;
+    }
   }
   return DELREC_OK;
 }
@@ -938,7 +927,6 @@ static int run_axstep(const delrec_layer* ly, const delrec_lif* lif, const float
 
 static size_t backward_ws(const delrec_layer* ly, int kind) {
   const BwdPlan bp = plan_backward(ly, kind);
-  const PairPlan pp = plan_pairs(ly, bp.mode, nullptr);
   const SrcPlan sp = plan_src(ly);
   const size_t N = ly->N, TBN = (size_t)ly->T * ly->B * N;
   Carve c(nullptr, (size_t)-1);
@@ -980,8 +968,7 @@ static size_t backward_ws(const delrec_layer* ly, int kind) {
       c.take<unsigned int>((size_t)h64.tiles);
     }
   }
-  const int parts = kind == DELREC_SYNAPTIC ? 3 : 1;
-  c.take<float>((size_t)pp.splits * N * N * parts);   // pair partials
+  if (kind == DELREC_SYNAPTIC) c.take<unsigned char>(dense_dw_ws(ly, 1, ly->L));   // lag correlation stack
   if (kind != DELREC_SYNAPTIC) {
     const size_t dws = dense_dw_ws(ly, bp.MM + 1, kind == DELREC_HYBRID ? ly->K + 1 : 1);
     c.take<unsigned char>(dws);
@@ -1137,9 +1124,6 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
   else rc = launch_bwd_mode<2>(a, bp, st);
   if (rc) return rc;
   // ---- parameter gradients
-  const PairPlan pp = plan_pairs(ly, bp.mode, nullptr);
-  const int parts = kind == DELREC_SYNAPTIC ? 3 : 1;
-  float* ppart = c.take<float>((size_t)pp.splits * N * N * parts);
   float* dsm = kind == DELREC_SYNAPTIC ? c.take<float>((size_t)N * N) : nullptr;
   const SrcPlan sp = plan_src(ly);
   float* spart = c.take<float>((size_t)sp.splits * N * (bp.TAPS + 1));
@@ -1180,29 +1164,27 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
     }
   } else {
     if (g->dW || g->dd || g->ds) {
-      // synaptic pair sums (per-synapse lags): dW, dd, ds
-      PairArgs pa{};
-      pa.T = T; pa.B = B; pa.N = N; pa.KR = pp.KR; pa.BCH = pp.BCH; pa.rows_per_split = pp.rows_per_split;
-      pa.gr = gr; pa.Y = y; pa.offT = offT; pa.dT = dT; pa.s = s; pa.W = W;
-      pa.Lm1 = ly->L - 1;
-      pa.NZ = pp.NZ;
-      const size_t nn = (size_t)N * N;
-      pa.out_dW = ppart;
-      pa.out_dd = ppart + (size_t)pp.splits * nn;
-      pa.out_ds = ppart + (size_t)2 * pp.splits * nn;
-      rc = launch_pairs(bp.mode, pa, pp, N, st);
+      // synaptic: the per-lag correlation stack on the tensor cores, then per synapse the
+      // triangle-weighted sums over its lag window: dW, dd, ds
+      const int nk = ly->L;
+      const size_t dws = dense_dw_ws(ly, 1, nk);
+      unsigned char* region = c.take<unsigned char>(dws);
+      Carve dc(region, dws);
+      DenseBufs dbf{};
+      if (!c.ok || !dense_carve(ly, 1, nk, nullptr, dc, &dbf)) return DELREC_ERR_WORKSPACE;
+      rc = syn_cstack(ly, gr, y, dbf, st);
       if (rc) return rc;
-      if (g->dW) {
-        k_sum_splits<<<grid_for(nn, 256), 256, 0, st>>>(pa.out_dW, pp.splits, nn, g->dW);
-        DR_LAUNCHED();
-      }
-      if (g->dd) {
-        k_sum_splits<<<grid_for(nn, 256), 256, 0, st>>>(pa.out_dd, pp.splits, nn, g->dd);
-        DR_LAUNCHED();
-      }
+      const size_t nn = (size_t)N * N;
+      float* dsmo = g->ds ? dsm : nullptr;
+      const int tw = syn_window(ly);
+      if (tw == 4)
+        k_syn_cstack_combine<4><<<grid_for(nn, 256), 256, 0, st>>>(N, ly->L - 1, dT, s, W, dbf.P, g->dW, g->dd, dsmo);
+      else if (tw == 8)
+        k_syn_cstack_combine<8><<<grid_for(nn, 256), 256, 0, st>>>(N, ly->L - 1, dT, s, W, dbf.P, g->dW, g->dd, dsmo);
+      else
+        k_syn_cstack_combine<16><<<grid_for(nn, 256), 256, 0, st>>>(N, ly->L - 1, dT, s, W, dbf.P, g->dW, g->dd, dsmo);
+      DR_LAUNCHED();
       if (g->ds) {
-        k_sum_splits<<<grid_for(nn, 256), 256, 0, st>>>(pa.out_ds, pp.splits, nn, dsm);
-        DR_LAUNCHED();
         k_colsum<<<cdiv(N, 128), 128, 0, st>>>(dsm, N, N, g->ds);
         DR_LAUNCHED();
       }

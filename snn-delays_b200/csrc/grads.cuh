@@ -1,19 +1,13 @@
 // Parameter-gradient reductions over the T*B rows, run after the reverse scan.
 //
-// k_pair_reduce  per-synapse correlations at per-synapse lags:
-//     acc_j[i,o] = sum_{t,b} gr[t,b,i] * Y[t - lag_io - j, b, o],  j < TW
-//   axonal   Y = z (axonal interpolation of the spikes), lag 0, TW 1      -> dW = acc
-//   hybrid   Y = z of the learned base, lag = offset k_io, TW 1         -> dW = acc
-//   synaptic Y = spikes, lag = first lag of the synapse's triangle window -> dW, dd, ds
-//            (the reference's per-lag Cstack, synaptic_eventdriven.py:453-468, restricted
-//            to the lags where the triangle or its derivatives are nonzero)
-//   A CTA owns a 32x32 tile of synapses; lane = source o, warp = 4 targets i, so the
-//   per-synapse lag never causes shared-memory bank conflicts.  The reduction over
-//   (t,b) is split across `gridDim.z` partial buffers summed afterwards in a fixed
-//   order (deterministic, no atomics).
-// k_source_reduce  per-neuron sums: db[n] = sum gr[.,.,n] and, for axonal/hybrid,
-//   dmask_n[j] = sum gz[t,b,n] y[t-l0-j,b,n] mapped to dd_n, ds_n through the closed-form
-//   triangle derivatives (recdel_base.py:337-342 + AxonalRecdelTriton.backward :421-435).
+// k_syn_cstack_combine  synaptic dW, dd, ds from the per-lag correlation stack
+//   C_l[i,o] = sum_{t,b} gr[t,b,i] y[t-l,b,o] (tensor-core GEMMs on the host side), over
+//   the lags of each synapse's triangle window (the reference's Cstack,
+//   synaptic_eventdriven.py:453-468).
+// k_source_pass / k_source_reduce  per-neuron sums: db[n] = sum gr[.,.,n] and, for
+//   axonal/hybrid, dmask_n[j] = sum gz[t,b,n] y[t-l0-j,b,n] mapped to dd_n, ds_n through
+//   the closed-form triangle derivatives (recdel_base.py:337-342 +
+//   AxonalRecdelTriton.backward :421-435).
 #pragma once
 
 #include <cuda_bf16.h>
@@ -22,140 +16,35 @@
 
 namespace delrec {
 
-struct PairArgs {
-  int T, B, N, KR, BCH, rows_per_split;
-  int NZ;                // hybrid: operand variants z_0..z_{NZ-1} (stride T*B*N)
-  const float* gr;       // (T,B,N) gradient at the recurrent input of the target
-  const float* Y;        // (T,B,N) delayed operand of the source
-  const uint8_t* offT;   // hybrid lags (o-major), or null
-  const float* dT;       // synaptic delays (o-major), or null
-  const float* s;        // synaptic half-widths per source
-  const float* W;        // (N,N) for synaptic dd/ds
-  int Lm1;
-  float* out_dW;         // [split][N][N]
-  float* out_dd;         // [split][N][N] synaptic
-  float* out_ds;         // [split][N][N] synaptic
-};
-
-// MODE 0 axonal, 1 hybrid, 2 synaptic
-template <int MODE, int TW, int BCHT>
-__global__ void __launch_bounds__(256) k_pair_reduce(PairArgs a) {
-  extern __shared__ __align__(16) float psm[];
-  const int N = a.N, B = a.B, T = a.T, BCH = BCHT, KR = a.KR;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int o0 = blockIdx.x * 32, i0 = blockIdx.y * 32;
-  const int o = o0 + lane;
-  float* G = psm;                         // [BCH][32]  gr rows of the tile's targets
-  float* Yr = psm + BCH * 32;             // [NZ][KR][BCH][32] ring of the sources' operand
-  const int NZ = MODE == 1 ? a.NZ : 1;
-  const size_t TBN = (size_t)T * B * N;
-  int lag[4], zsel[4];
-  float acc[4][TW];
+// Synaptic parameter gradients from the per-lag correlation stack (the reference's Cstack,
+// synaptic_eventdriven.py:453-468), computed for all lags on the tensor cores:
+//   C_l[i, o] = sum_{t,b} gr[t, b, i] y[t - l, b, o],   l = 0..L-1,
+// combined over each synapse's lag window (TW lags from max(1, floor(1+d-s) - 1)):
+//   dW = sum_l h(l) C_l,  dd = W sum_l dh/dd(l) C_l,  dsm = W sum_l dh/ds(l) C_l.
+template <int TW>
+__global__ void k_syn_cstack_combine(int N, int Lm1, const float* __restrict__ dT, const float* __restrict__ s,
+                                     const float* __restrict__ W, const float* __restrict__ C,
+                                     float* __restrict__ dW, float* __restrict__ dd, float* __restrict__ dsm) {
+  const size_t nn = (size_t)N * N;
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < nn; e += (size_t)gridDim.x * blockDim.x) {
+    const int i = (int)(e / N), o = (int)(e % N);
+    const Tri tr = make_tri(dT[(size_t)o * N + i], s[o]);
+    const int lo = (int)floorf(__fsub_rn(tr.onepd, tr.s)) - 1;
+    const int lag = lo < 1 ? 1 : lo;
+    float dw = 0.f, gdd = 0.f, gds = 0.f;
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const int i = i0 + warp * 4 + q;
-    lag[q] = 0;
-    zsel[q] = 0;
-    if (i < N && o < N) {
-      if (MODE == 1) {
-        lag[q] = a.offT[(size_t)o * N + i];
-        zsel[q] = lag[q] < NZ - 1 ? lag[q] : NZ - 1;
-      }
-      if (MODE == 2) {
-        const Tri tr = make_tri(a.dT[(size_t)o * N + i], a.s[o]);
-        int lo = (int)floorf(__fsub_rn(tr.onepd, tr.s)) - 1;
-        lag[q] = lo < 1 ? 1 : lo;
-      }
+    for (int j = 0; j < TW; ++j) {
+      const int l = lag + j;
+      if (l > Lm1) break;
+      const float c = C[(size_t)l * nn + e];
+      dw = fmaf(tri_h(tr, l), c, dw);
+      gdd = fmaf(tri_dh_dd(tr, l), c, gdd);
+      gds = fmaf(tri_dh_ds(tr, l), c, gds);
     }
-#pragma unroll
-    for (int j = 0; j < TW; ++j) acc[q][j] = 0.f;
-  }
-  // rows handled by this split: b-chunks [bc0, bc1)
-  const int nbc = cdiv(B, BCH);
-  const int bc0 = blockIdx.z * a.rows_per_split, bc1 = min(nbc, bc0 + a.rows_per_split);
-  constexpr int EPT = BCHT / 8;  // staged elements per thread per array (256 threads)
-  constexpr int NZMAX = MODE == 1 ? 4 : 1;
-  float pg[EPT], py[NZMAX][EPT];
-  auto prefetch = [&](int t, int b0) {
-#pragma unroll
-    for (int r = 0; r < EPT; ++r) {
-      const int e = threadIdx.x + r * 256;
-      const int bl = e >> 5, c = e & 31;
-      const int b = b0 + bl;
-      const size_t row = ((size_t)t * B + b) * N;
-      const bool okb = b < B;
-      pg[r] = (okb && i0 + c < N) ? __ldg(a.gr + row + i0 + c) : 0.f;
-#pragma unroll
-      for (int z = 0; z < NZMAX; ++z)
-        if (z < NZ) py[z][r] = (okb && o0 + c < N) ? __ldg(a.Y + z * TBN + row + o0 + c) : 0.f;
-    }
-  };
-  for (int bc = bc0; bc < bc1; ++bc) {
-    const int b0 = bc * BCH;
-    for (int e = threadIdx.x; e < NZ * KR * BCH * 32; e += blockDim.x) Yr[e] = 0.f;
-    prefetch(0, b0);
-    __syncthreads();
-    for (int t = 0; t < T; ++t) {
-      const int slot = t & (KR - 1);
-#pragma unroll
-      for (int r = 0; r < EPT; ++r) {
-        const int e = threadIdx.x + r * 256;
-        G[e] = pg[r];
-#pragma unroll
-        for (int z = 0; z < NZMAX; ++z)
-          if (z < NZ) Yr[((size_t)z * KR + slot) * BCH * 32 + e] = py[z][r];
-      }
-      __syncthreads();
-      if (t + 1 < T) prefetch(t + 1, b0);
-#pragma unroll 4
-      for (int bl = 0; bl < BCH; ++bl) {
-        const float4 g4 = *(const float4*)(G + bl * 32 + warp * 4);
-        const float gg[4] = {g4.x, g4.y, g4.z, g4.w};
-        if (MODE == 0) {
-          const float yv = Yr[slot * BCH * 32 + bl * 32 + lane];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) acc[q][0] = fmaf(gg[q], yv, acc[q][0]);
-        } else {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-#pragma unroll
-            for (int j = 0; j < TW; ++j) {
-              const int sl = (t - lag[q] - j) & (KR - 1);
-              // a slot of a negative time is still zero (ring zeroed per chunk, and a
-              // slot is only written at its own time); lag + j < KR by construction
-              acc[q][j] = fmaf(gg[q], Yr[(((size_t)zsel[q] * KR + sl) * BCH + bl) * 32 + lane], acc[q][j]);
-            }
-          }
-        }
-      }
-      __syncthreads();
-    }
-  }
-  // ---- finalize this split's partial results
-  const size_t pbase = (size_t)blockIdx.z * N * N;
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const int i = i0 + warp * 4 + q;
-    if (i >= N || o >= N) continue;
-    const size_t idx = pbase + (size_t)i * N + o;
-    if (MODE != 2) {
-      a.out_dW[idx] = acc[q][0];
-    } else {
-      const Tri tr = make_tri(a.dT[(size_t)o * N + i], a.s[o]);
-      const float w = a.W[(size_t)i * N + o];
-      float dw = 0.f, gdd = 0.f, gds = 0.f;
-#pragma unroll
-      for (int j = 0; j < TW; ++j) {
-        const int l = lag[q] + j;
-        if (l > a.Lm1) break;
-        dw = fmaf(tri_h(tr, l), acc[q][j], dw);
-        gdd = fmaf(tri_dh_dd(tr, l), acc[q][j], gdd);
-        gds = fmaf(tri_dh_ds(tr, l), acc[q][j], gds);
-      }
-      a.out_dW[idx] = dw;
-      a.out_dd[idx] = __fmul_rn(w, gdd);
-      a.out_ds[idx] = __fmul_rn(w, gds);
-    }
+    if (dW) dW[e] = dw;
+    const float w = W[e];
+    if (dd) dd[e] = __fmul_rn(w, gdd);
+    if (dsm) dsm[e] = __fmul_rn(w, gds);
   }
 }
 
