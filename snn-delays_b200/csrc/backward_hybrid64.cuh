@@ -165,6 +165,7 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid64(Hyb64Args a) {
   bool pin[PPT], pok[PPT];   // pair inside the block's slice x tile; and a real sample
   float lam[PPT], kp[PPT];
   float pf_gy[PPT], pf_u[PPT], pf_tap[PPT][TPF];
+  LifPre pf_pre[PPT];   // u-only part of the LIF backward of the prefetched step
 #pragma unroll
   for (int k = 0; k < PPT; ++k) {
     const int p = tid + k * NTH;
@@ -210,6 +211,8 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid64(Hyb64Args a) {
   };
   prefetch_lif(T - 1);
   prefetch_taps(T - 1);
+#pragma unroll
+  for (int k = 0; k < PPT; ++k) pf_pre[k] = lif_bwd_prep(pf_u[k], a.lif);
 
   const uint32_t gbase = (uint32_t)__cvta_generic_to_shared(grc) + lane * 8;
   const int ol_w = warp;   // the warp's source
@@ -223,11 +226,12 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid64(Hyb64Args a) {
   const size_t xtile = (size_t)N * BT;
 
   for (int t = T - 1; t >= 0; --t) {
-    float cur_gy[PPT], cur_u[PPT], cur_tap[PPT][TPF];
+    float cur_gy[PPT], cur_tap[PPT][TPF];
+    LifPre cur_pre[PPT];
 #pragma unroll
     for (int k = 0; k < PPT; ++k) {
       cur_gy[k] = pf_gy[k];
-      cur_u[k] = pf_u[k];
+      cur_pre[k] = pf_pre[k];
 #pragma unroll
       for (int j = 0; j < TPF; ++j) cur_tap[k][j] = pf_tap[k][j];
     }
@@ -252,7 +256,7 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid64(Hyb64Args a) {
           }
         }
         const float gY = __fadd_rn(cur_gy[k], gfut);
-        const float du = lif_backward(gY, cur_u[k], lam[k], a.lif);
+        const float du = lif_backward_pre(gY, lam[k], cur_pre[k], a.lif);
         lam[k] = lif_carry(du, a.lif);
         grv = __fmul_rn(du, kp[k]);
         const size_t idx = ((size_t)t * B + b0 + bl) * N + o0 + ol;
@@ -296,6 +300,9 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid64(Hyb64Args a) {
         }
     }
     prefetch_taps(t - 1);
+    // the u-only part of step t-1's LIF backward (its u arrived during this step)
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) pf_pre[k] = lif_bwd_prep(pf_u[k], a.lif);
     // ===== W: the tile's gr(t)
     if (tid == 0) {
       long long polls = 0;

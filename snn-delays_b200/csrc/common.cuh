@@ -101,6 +101,30 @@ __device__ __forceinline__ float lif_backward(float gY, float u, float lam, cons
   const float gS = p.detach ? gY : __fadd_rn(gY, __fmul_rn(lam, __fsub_rn(p.vr, u)));
   return __fadd_rn(s ? 0.f : lam, __fmul_rn(gS, sg));
 }
+// lif_backward split in two: the part that depends on u only (surrogate derivative, spike,
+// reset term), computed ahead of time, and the part that needs the incoming gradient.
+// lif_backward_pre(gY, lam, lif_bwd_prep(u, p), p) == lif_backward(gY, u, lam, p) bit for bit.
+struct LifPre {
+  float sg;     // surrogate derivative at u - vth
+  float vr_u;   // vr - u (hard reset)
+  bool s;       // spike
+};
+__device__ __forceinline__ LifPre lif_bwd_prep(float u, const LifK& p) {
+  LifPre q;
+  const float x = __fsub_rn(u, p.vth);
+  q.s = x >= 0.f;
+  q.sg = surrogate_grad(x, p);
+  q.vr_u = __fsub_rn(p.vr, u);
+  return q;
+}
+__device__ __forceinline__ float lif_backward_pre(float gY, float lam, const LifPre& q, const LifK& p) {
+  if (p.soft) {
+    const float gS = p.detach ? gY : __fsub_rn(gY, __fmul_rn(lam, p.vth));
+    return __fadd_rn(lam, __fmul_rn(gS, q.sg));
+  }
+  const float gS = p.detach ? gY : __fadd_rn(gY, __fmul_rn(lam, q.vr_u));
+  return __fadd_rn(q.s ? 0.f : lam, __fmul_rn(gS, q.sg));
+}
 __device__ __forceinline__ float lif_carry(float du, const LifK& p) {
   return __fmul_rn(p.decay, du);
 }
