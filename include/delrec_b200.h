@@ -212,6 +212,11 @@ int delrec_linear_backward(int M, int K, int N, const float* x, const float* W, 
                            int x_binary, float* dx, float* dW, float* dbias, void* workspace,
                            size_t workspace_bytes, void* stream);
 
+/* Sets *count (device) to the number of entries of x[0..n) that are neither 0 nor 1;
+ * asynchronous on the stream, x 16-byte aligned.  The projections' spike-input test
+ * (x_binary above); no counterpart in the reference, whose projections are fp32 GEMMs. */
+int delrec_count_nonbinary(const float* x, size_t n, unsigned int* count, void* stream);
+
 /* ---- device status word ------------------------------------------------------------ */
 /* Kernels record internal inconsistencies (an out-of-range lag or index that was
  * skipped) in a device status word instead of trapping.  Reading it synchronizes. */

@@ -1296,6 +1296,15 @@ int delrec_hybrid_backward(const delrec_layer* ly, const delrec_lif* lif, const 
   return run_backward(ly, DELREC_HYBRID, lif, gy, u, y, W, base, offsets, s, keep, g, ws, wsb, (cudaStream_t)stream);
 }
 
+int delrec_count_nonbinary(const float* x, size_t n, unsigned int* count, void* stream) {
+  if (!count || (n && !x) || ((uintptr_t)x & 15) != 0) return DELREC_ERR_ARG;
+  const cudaStream_t st = (cudaStream_t)stream;
+  DR_CUDA(cudaMemsetAsync(count, 0, sizeof(unsigned int), st));
+  if (n == 0) return DELREC_OK;
+  k_count_nonbinary<<<grid_for(n / 4 + 1, 256), 256, 0, st>>>(x, n, count);
+  DR_LAUNCHED();
+  return DELREC_OK;
+}
 size_t delrec_linear_forward_workspace(int M, int K, int N, int x_binary) {
   return (M > 0 && K > 0 && N > 0) ? linear_fwd_ws(M, K, N, x_binary ? 1 : 0) : 0;
 }

@@ -169,6 +169,23 @@ __global__ void k_fill_f32(float* __restrict__ p, size_t n, float value) {
     p[e] = value;
 }
 
+// *count += number of entries of x[0..n) that are neither 0 nor 1 (x 16-byte aligned)
+__global__ void k_count_nonbinary(const float* __restrict__ x, size_t n, unsigned int* __restrict__ count) {
+  unsigned int c = 0;
+  const size_t n4 = n / 4;
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n4; e += (size_t)gridDim.x * blockDim.x) {
+    const float4 v = __ldcs((const float4*)x + e);
+    c += !(v.x == 0.f || v.x == 1.f);
+    c += !(v.y == 0.f || v.y == 1.f);
+    c += !(v.z == 0.f || v.z == 1.f);
+    c += !(v.w == 0.f || v.w == 1.f);
+  }
+  for (size_t e = n4 * 4 + blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x)
+    c += !(x[e] == 0.f || x[e] == 1.f);
+  for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(0xffffffffu, c, off);
+  if ((threadIdx.x & 31) == 0 && c) atomicAdd(count, c);
+}
+
 // dW[n*K + c] = D[n][c] + D[Np+n][c] + D[2Np+n][c];  dbias[n] = the same at c = K.
 // D is (3*Np, Kp) row-major (the column-major Kp x 3Np GEMM output).
 __global__ void k_linear_dw_reduce(int N, int K, int Np, int Kp, const float* __restrict__ D,

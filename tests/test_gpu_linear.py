@@ -81,3 +81,20 @@ def test_broken_spike_promise_sets_status():
     torch.cuda.synchronize()
     assert _lib.status() != 0
     _lib.lib().delrec_clear_status()
+
+
+def test_spike_input_check():
+    """delrec_count_nonbinary: exact on 0/1 inputs, any other value (here one entry, in a
+    ragged tail, and an unaligned view) is detected."""
+    from delrec.linear import _is_binary
+    g = torch.Generator().manual_seed(3)
+    for n in (1, 7, 4096, 64001):
+        x = (torch.rand(n, generator=g) < 0.3).float().cuda()
+        assert _is_binary(x)
+        y = x.clone()
+        y[n - 1] = 0.5
+        assert not _is_binary(y)
+    z = (torch.rand(1001, generator=g) < 0.3).float().cuda()
+    assert _is_binary(z[1:])
+    z[500] = 2.0
+    assert not _is_binary(z[1:])
