@@ -250,7 +250,6 @@ __global__ void __launch_bounds__(512, 1) k_bwd_axonal_mma(AxMmaArgs a) {
   bool pin[PPT], pok[PPT];
   float lam[PPT], kp[PPT];
   float pf_gy[PPT], pf_u[PPT], pf_tap[PPT][TPF];
-  LifPre pf_pre[PPT];   // u-only part of the LIF backward of the prefetched step
 #pragma unroll
   for (int k = 0; k < PPT; ++k) {
     const int p = tid + k * NTH;
@@ -295,8 +294,6 @@ __global__ void __launch_bounds__(512, 1) k_bwd_axonal_mma(AxMmaArgs a) {
   };
   prefetch_lif(T - 1);
   prefetch_taps(T - 1);
-#pragma unroll
-  for (int k = 0; k < PPT; ++k) pf_pre[k] = lif_bwd_prep(pf_u[k], a.lif);
 
   const int nt8 = warp & 7, kh = warp >> 3, g = lane >> 2, c = lane & 3;
   // ring cells of this lane's C values: sources g and g+8, samples nt8*8 + 2c (+1)
@@ -337,12 +334,11 @@ __global__ void __launch_bounds__(512, 1) k_bwd_axonal_mma(AxMmaArgs a) {
   };
 
   for (int t = T - 1; t >= 0; --t) {
-    float cur_gy[PPT], cur_tap[PPT][TPF];
-    LifPre cur_pre[PPT];
+    float cur_gy[PPT], cur_u[PPT], cur_tap[PPT][TPF];
 #pragma unroll
     for (int k = 0; k < PPT; ++k) {
       cur_gy[k] = pf_gy[k];
-      cur_pre[k] = pf_pre[k];
+      cur_u[k] = pf_u[k];
 #pragma unroll
       for (int j = 0; j < TPF; ++j) cur_tap[k][j] = pf_tap[k][j];
     }
@@ -367,7 +363,7 @@ __global__ void __launch_bounds__(512, 1) k_bwd_axonal_mma(AxMmaArgs a) {
           }
         }
         const float gY = __fadd_rn(cur_gy[k], gfut);
-        const float du = lif_backward_pre(gY, lam[k], cur_pre[k], a.lif);
+        const float du = lif_backward(gY, cur_u[k], lam[k], a.lif);
         lam[k] = lif_carry(du, a.lif);
         grv = __fmul_rn(du, kp[k]);
         const size_t idx = ((size_t)t * B + b0 + bl) * N + o0 + ol;
@@ -396,9 +392,6 @@ __global__ void __launch_bounds__(512, 1) k_bwd_axonal_mma(AxMmaArgs a) {
         }
     }
     prefetch_taps(t - 1);
-    // the u-only part of step t-1's LIF backward (its u arrived during this step)
-#pragma unroll
-    for (int k = 0; k < PPT; ++k) pf_pre[k] = lif_bwd_prep(pf_u[k], a.lif);
     // ===== W: the tile's gr(t), staged as bf16 pieces
     if (tid == 0) {
       long long polls = 0;
