@@ -173,7 +173,7 @@ __device__ __forceinline__ uint32_t hist_window(uint64_t h0, uint64_t h1, int p0
   return (uint32_t)((h0 >> p0) | (h1 << (64 - p0)));
 }
 template <int TAPSMAX, int MMX>
-__global__ void __launch_bounds__(256, 3) k_source_pass(SrcArgs a, int want_z, int warm, __nv_bfloat16* __restrict__ zh) {
+__global__ void __launch_bounds__(256, 2) k_source_pass(SrcArgs a, int want_z, int warm, __nv_bfloat16* __restrict__ zh) {
   __shared__ float sred[8][32][TAPSMAX + 1];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int n = blockIdx.x * 32 + lane;
@@ -223,7 +223,7 @@ __global__ void __launch_bounds__(256, 3) k_source_pass(SrcArgs a, int want_z, i
       }
     }
     // outputs te in [c0, c1), inputs t_in = te + MM
-    constexpr int U = 4;
+    constexpr int U = 8;
     for (int t0 = c0; t0 < c1; t0 += U) {
       float g[U], yv[U], gzv[U][MMX + 1];
 #pragma unroll
