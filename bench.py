@@ -65,6 +65,9 @@ def make_config(spec, B):
     cfg.hybrid_offset_scale = spec["offsets"]
     cfg.hybrid_base_centering = "normal"
     cfg.sigma_init = 0.0
+    # the synthetic inputs' kind is known: Bernoulli spike trains or real values, so the
+    # first projection needs no per-call 0/1 test (and no host synchronisation per step)
+    cfg.input_spikes = spec["rate"] is not None and spec.get("input") != "normal"
     return cfg
 
 

@@ -67,9 +67,13 @@ class spike_registrator(torch.nn.Module):
 
 def _spike_input(config, idx):
     """The input of the idx-th projection is a spike train (0/1) when a spiking layer
-    feeds it directly; the first projection's data is tested per call (None)."""
+    feeds it directly.  The first projection's data is tested on every call (None), which
+    costs a read of the test's result (a synchronisation) per forward, unless the optional
+    ``config.input_spikes`` declares it: True for datasets of 0/1 spike trains (checked on
+    the device through the status word), False for real-valued inputs."""
     if idx == 0:
-        return None
+        v = getattr(config, "input_spikes", None)
+        return None if v is None else bool(v)
     return False if config.use_batch_norm else True
 
 

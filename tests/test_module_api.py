@@ -184,3 +184,18 @@ def test_maximum_positive_keeps_axonal_delay_budget(hybrid_name, axonal_name):
     offsets = [b for n, b in h.named_buffers() if n.endswith(".offsets")]
     assert offsets and all(not b.requires_grad for b in offsets)
     assert all(int(b.max()) <= 4 and int(b.min()) >= 0 for b in offsets)
+
+
+def test_declared_input_spikes_reach_the_first_projection():
+    """config.input_spikes (optional) sets the first projection's binary_input: unset ->
+    tested per call (None), True -> spike path, False -> real-valued path; the later
+    projections read spikes from a spiking layer either way."""
+    from delrec import networks
+    for flag, want in ((None, None), (True, True), (False, False)):
+        cfg = mem_config(hidden=[16, 8], bias=False)
+        if flag is not None:
+            cfg.input_spikes = flag
+        model = networks.SNN_axonal_recurrent_delays(cfg)
+        lins = [m for m in model.layers if type(m).__name__ == "Linear"]
+        assert lins[0].binary_input == want
+        assert all(m.binary_input is True for m in lins[1:])
