@@ -851,7 +851,10 @@ static int run_linear_backward(int M, int K, int N, const float* x, const float*
   float* D = c.take<float>((size_t)3 * p.Np * p.Kp);
   void* cws = c.take<unsigned char>(kCublasWs);
   if (!c.ok) return DELREC_ERR_WORKSPACE;
-  k_pack_rows<<<grid_for((size_t)M * p.Np / 8, 256), 256, 0, st>>>(M, N, p.Np, gout, N, nullptr, 0, 6, kPatReal6,
+  // G' = [g0 g1 g2 g0 g1 g0]; the weight-gradient products read only its first three blocks,
+  // so without dx the last three are not written (gb: blocks per row of G')
+  const int gb = dx ? 6 : 3;
+  k_pack_rows<<<grid_for((size_t)M * p.Np / 8, 256), 256, 0, st>>>(M, N, p.Np, gout, N, nullptr, 0, gb, kPatReal6,
                                                                    0, G);
   DR_LAUNCHED();
   cublasHandle_t h;
@@ -871,7 +874,7 @@ static int run_linear_backward(int M, int K, int N, const float* x, const float*
     // column-major: D (Kp x 3Np) = sum_a X_a-view (Kp x M) . G'-view^T (M x (3-a)Np)
     for (int a = 0; a < p.nbx; ++a) {
       rc = gemm_bf16(h, CUBLAS_OP_N, CUBLAS_OP_T, p.Kp, (3 - a) * p.Np, M, X + (size_t)a * p.Kp, p.nbx * p.Kp, G,
-                     6 * p.Np, a == 0 ? 0.f : 1.f, D, p.Kp);
+                     gb * p.Np, a == 0 ? 0.f : 1.f, D, p.Kp);
       if (rc) return rc;
     }
     k_linear_dw_reduce<<<grid_for((size_t)N * (K + 1), 256), 256, 0, st>>>(N, K, p.Np, p.Kp, D, dW, dbias);
