@@ -2,7 +2,7 @@
 
 Run here (it needs the read-only reference checkout; the GPU box never runs it):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path of the reference checkout>
 
 For every case it runs, on identical seeded inputs,
   * the reference's canonical pure-PyTorch scans ``multi_step_forward_v2``
@@ -24,7 +24,9 @@ os.environ["TRITON_INTERPRET"] = "1"
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+if len(sys.argv) < 2:
+    sys.exit("usage: python tests/golden/make_golden.py <path of the reference checkout>")
+REF = sys.argv[1]
 sys.path.insert(0, os.path.join(REF, "src"))
 sys.path.insert(0, REPO)
 
