@@ -124,8 +124,10 @@ int delrec_axonal_backward(const delrec_layer* layer, const delrec_lif* lif,
  * callers that cannot call cudaMalloc while the layer runs (all device memory handed to
  * their own allocator, no device-wide synchronisation allowed in the loop, or a plugin
  * host that forbids allocation after start-up).  Its scratch is a fixed 8 MiB device
- * array inside the library (N <= 1024 neurons; larger layers get DELREC_ERR_WORKSPACE),
- * held by every GPU that loads the library until the process exits.  The first call on
+ * array inside the library, held by every GPU that loads the library until the process
+ * exits.  Limits: N <= 1024 neurons (wider layers get DELREC_ERR_WORKSPACE); every width
+ * runs the per-sample scan, whose spike history lives in shared memory, so very long
+ * rings (at N = 1024, L above about 1000) get DELREC_ERR_UNSUPPORTED.  The first call on
  * a device looks the array up (cudaGetSymbolAddress), so make that first call before any
  * stream capture.  All calls share the array: calls that overlap on the GPU (other
  * streams, other threads) race on it.  Every byte it reads is written earlier in the

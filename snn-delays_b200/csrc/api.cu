@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
+#include <mutex>
 #include <cstdio>
 #include <cstring>
 
@@ -1417,31 +1419,44 @@ int delrec_dcls_backward(int T, int B, int Cin, int Cout, int groups, int K, int
 // runtime that forbids allocation after start-up.  For them the scratch of the axonal
 // forward (transposed weights and the per-source tap table) lives in this fixed device
 // array, which every GPU that loads the library holds until the process exits.
-static constexpr size_t kNoAllocScratchBytes = 8u << 20;   // 8 MiB: N <= 1024 neurons
+static constexpr size_t kNoAllocScratchBytes = 8u << 20;   // 8 MiB
+static constexpr int kNoAllocMaxN = 1024;                  // widest layer it accepts
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
-static void* g_noalloc_ptr[64] = {nullptr};
+static std::atomic<void*> g_noalloc_ptr[64];
+static std::mutex g_noalloc_mu;
 
 int delrec_axonal_forward_noalloc(const delrec_layer* ly, const delrec_lif* lif, const float* x,
                                   const float* W, const float* bias, const float* d, const float* s,
                                   const float* keep, float* y, float* u, void* stream) {
   if (!ly) return DELREC_ERR_ARG;
-  if (forward_ws(ly, DELREC_AXONAL, false) > kNoAllocScratchBytes) {
-    fprintf(stderr, "delrec_b200: delrec_axonal_forward_noalloc needs %zu bytes of scratch for N=%d, "
-                    "more than its fixed %zu-byte array; use delrec_axonal_forward with a workspace\n",
-            forward_ws(ly, DELREC_AXONAL, false), (int)ly->N, kNoAllocScratchBytes);
+  if (ly->N > kNoAllocMaxN || forward_ws(ly, DELREC_AXONAL, false) > kNoAllocScratchBytes) {
+    fprintf(stderr, "delrec_b200: delrec_axonal_forward_noalloc supports N <= %d neurons (its fixed "
+                    "%zu-byte scratch array); N=%d needs the workspace entry point delrec_axonal_forward\n",
+            kNoAllocMaxN, kNoAllocScratchBytes, (int)ly->N);
     return DELREC_ERR_WORKSPACE;
+  }
+  // the per-sample scan keeps the spike history of its sample in shared memory
+  if (ly->N >= 1 && ly->L >= 1 && plan_forward(ly, DELREC_AXONAL).smem > kSmemLimit) {
+    fprintf(stderr, "delrec_b200: delrec_axonal_forward_noalloc: ring length L=%d is too long for the "
+                    "per-sample scan at N=%d\n", (int)ly->L, (int)ly->N);
+    return DELREC_ERR_UNSUPPORTED;
   }
   int dev = 0;
   DR_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return DELREC_ERR_UNSUPPORTED;
-  if (!g_noalloc_ptr[dev]) {
-    // once per device, with that device current: the symbol's device address
-    void* p = nullptr;
-    DR_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-    g_noalloc_ptr[dev] = p;
+  void* scratch = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (!scratch) {
+    // once per device, with that device current: the symbol's device address (host
+    // threads making their first call together take turns here)
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    scratch = g_noalloc_ptr[dev].load(std::memory_order_relaxed);
+    if (!scratch) {
+      DR_CUDA(cudaGetSymbolAddress(&scratch, g_noalloc_scratch));
+      g_noalloc_ptr[dev].store(scratch, std::memory_order_release);
+    }
   }
   // the per-sample scan only: the step-by-step forward of wide layers needs more scratch
-  return run_forward(ly, DELREC_AXONAL, lif, x, W, bias, d, nullptr, s, keep, y, u, g_noalloc_ptr[dev],
+  return run_forward(ly, DELREC_AXONAL, lif, x, W, bias, d, nullptr, s, keep, y, u, scratch,
                      kNoAllocScratchBytes, (cudaStream_t)stream, false);
 }
 
