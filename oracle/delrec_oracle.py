@@ -33,6 +33,10 @@ CPU.  It is written from the reference's documented equations, not copied:
 * recurrent dropout: one keep-mask (values 0 or 1/(1-p)) per forward, applied to
   (rec + bias) at every step (delay_layers_triton.py:37-48, delay_layers_pytorch.py:179)
 
+The functions are device-agnostic torch code: the parity tests evaluate them in float64 on
+the CPU for small cases and, for the full BASELINE-shaped cases (where the CPU would take
+hours), in float64 on the GPU; either way they are the checker, never the product.
+
 Parity pin: ``tests/golden/make_golden.py`` runs the reference's own v2 scans (imported
 unmodified) and its own Triton kernels (under the Triton CPU interpreter) on seeded
 inputs; ``tests/test_oracle_golden.py`` checks this oracle against those fixtures.
@@ -142,14 +146,14 @@ class OracleLIF:
 # triangular delay kernel
 # ----------------------------------------------------------------------------------
 
-def spread(sigma, p_spread, use_sig_p, dtype=torch.float32):
+def spread(sigma, p_spread, use_sig_p, dtype=torch.float32, device=None):
     """Half-width s of the triangle: a 0-d tensor, or (N,) per source under use_sig_p.
 
     Returns (s, s_max) with s_max a 0-d tensor."""
     if use_sig_p:
         s = 1.0 + 2.0 * sigma * torch.sigmoid(p_spread).to(dtype)
         return s, s.max()
-    s = torch.tensor(1.0 + float(sigma), dtype=dtype)
+    s = torch.tensor(1.0 + float(sigma), dtype=dtype, device=device)
     return s, s
 
 
@@ -161,7 +165,7 @@ def ring_length(d, s_max) -> int:
 def triangle(d, s, L):
     """h[..., l] = max(0, s - |l - (1 + d)|) / s^2 for l = 0..L-1; ``s`` broadcasts
     against ``d`` (append the lag axis yourself for per-source widths)."""
-    lags = torch.arange(L, dtype=d.dtype)
+    lags = torch.arange(L, dtype=d.dtype, device=d.device)
     return torch.clamp(s - torch.abs(lags - (1.0 + d)[..., None]), min=0.0) / (s * s)
 
 
@@ -181,7 +185,7 @@ def axonal_scan(x, W, d, lif: OracleLIF, sigma=0.0, p_spread=None, use_sig_p=Fal
     source j; d (N,) per source.  Returns y (T,B,N) [, u (T,B,N)]."""
     T, B, N = x.shape
     d = _prepare_d(d.to(x.dtype), round_delays)
-    s, s_max = spread(sigma, p_spread, use_sig_p, x.dtype)
+    s, s_max = spread(sigma, p_spread, use_sig_p, x.dtype, x.device)
     L = ring_length(d, s_max)
     sj = s[:, None] if use_sig_p else s
     h = triangle(d, sj, L)                       # (N, L), h[j, l]
@@ -213,7 +217,7 @@ def synaptic_scan(x, W, d, lif: OracleLIF, sigma=0.0, p_spread=None, use_sig_p=F
     indexed by the source o."""
     T, B, N = x.shape
     d = _prepare_d(d.to(x.dtype), round_delays)
-    s, s_max = spread(sigma, p_spread, use_sig_p, x.dtype)
+    s, s_max = spread(sigma, p_spread, use_sig_p, x.dtype, x.device)
     L = ring_length(d, s_max)
     so = s[None, :, None] if use_sig_p else s
     h = triangle(d, so, L)                       # (N, N, L), h[i, o, l]
@@ -275,7 +279,7 @@ def closed_form_delay_grad(C, W, d, sigma):
     """dd[i,o] = W[i,o] * sum_l C[i,o,l] * sign(l-1-d) / s^2 where |l-1-d| <= s."""
     s = 1.0 + float(sigma)
     lm = C.shape[-1]
-    a = torch.arange(lm, dtype=d.dtype).view(1, 1, lm) - 1.0 - d.unsqueeze(-1)
+    a = torch.arange(lm, dtype=d.dtype, device=d.device).view(1, 1, lm) - 1.0 - d.unsqueeze(-1)
     g = torch.sign(a) * (a.abs() <= s).to(d.dtype) / (s * s)
     return (W.unsqueeze(-1) * C * g).sum(-1)
 
@@ -291,7 +295,7 @@ def dcls_gauss_kernel(weight, P, SIG, dilated_kernel_size):
     dense kernel (Cout, Cin_g, K): w * g(k) / (sum_k g(k) + eps),
     g(k) = exp(-0.5 ((k - (P + K//2)) / (|SIG| + eps))^2)."""
     K = int(dilated_kernel_size)
-    k = torch.arange(K, dtype=weight.dtype)
+    k = torch.arange(K, dtype=weight.dtype, device=weight.device)
     c = P[0, :, :, 0] + K // 2                      # (Cout, Cin_g)
     sg = SIG[0, :, :, 0].abs() + 1e-7
     g = torch.exp(-0.5 * ((k - c[..., None]) / sg[..., None]) ** 2)

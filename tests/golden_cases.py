@@ -24,11 +24,12 @@ def surrogate(meta):
     return O.ATanSpike(2.0) if meta["surr"] == "atan" else O.TriangleSpike(1.0)
 
 
-def oracle_run(case, dtype=torch.float32):
+def oracle_run(case, dtype=torch.float32, device="cpu"):
     """Forward + BPTT of one golden case through the oracle; returns a dict like the
-    fixture's ``v2`` entry."""
+    fixture's ``v2`` entry (tensors on the CPU).  ``device``/``dtype`` choose where and in
+    which precision the oracle's torch code is evaluated."""
     meta, inp = case["meta"], case["inputs"]
-    c = lambda t: None if t is None else t.to(dtype).clone()
+    c = lambda t: None if t is None else t.to(device=device, dtype=dtype).clone()
     x = c(inp["x"]).requires_grad_(True)
     W = c(inp["W"]).requires_grad_(True)
     base = c(inp["d"]).requires_grad_(True)
@@ -51,4 +52,18 @@ def oracle_run(case, dtype=torch.float32):
         out["dp"] = p.grad
     if b is not None:
         out["dbias"] = b.grad
-    return out
+    return {k: v.cpu() for k, v in out.items()}
+
+
+def subset_case(case, samples):
+    """The same case restricted to the given batch samples (samples are independent, so
+    every per-sample quantity is unchanged and the parameter gradients are the sums over
+    the kept samples)."""
+    idx = torch.as_tensor(list(samples), dtype=torch.long)
+    inp = dict(case["inputs"])
+    inp["x"] = inp["x"][:, idx].contiguous()
+    inp["gy"] = inp["gy"][:, idx].contiguous()
+    if inp.get("keep") is not None:
+        inp["keep"] = inp["keep"][idx].contiguous()
+    meta = dict(case["meta"], B=int(idx.numel()))
+    return dict(meta=meta, inputs=inp)

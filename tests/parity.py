@@ -58,3 +58,14 @@ def compare_grads(got: dict, ref: dict, keys, rtol=GRAD_RTOL):
         out[k] = e
         assert e < rtol, f"gradient {k}: relative error {e:.3e} >= {rtol}"
     return out
+
+
+def mismatch_samples(y, y_ref):
+    """Batch samples whose spike trains differ anywhere (after compare_scan has checked
+    that every first difference is a near-tie)."""
+    d = (y.detach().cpu() != y_ref.detach().cpu()).any(0).any(-1)
+    return d.nonzero().flatten().tolist()
+
+
+def grad_keys(meta, has_bias):
+    return ["dx", "dW", "dd"] + (["dp"] if meta["use_sig_p"] else []) + (["dbias"] if has_bias else [])
