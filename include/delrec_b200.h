@@ -120,6 +120,21 @@ int delrec_axonal_backward(const delrec_layer* layer, const delrec_lif* lif,
                            const float* keep, const delrec_grads* grads,
                            void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- the library's own tensor-core GEMM (tcgen05, bf16 pieces, fp32 accumulate) ------
+ * No reference counterpart as an interface: it is the contraction engine behind the
+ * weight gradients, the lag-correlation stack and the projections (which the reference
+ * runs as torch matmuls / cuBLAS), exposed so it can be tested on its own.
+ * D (M,N) = [D +] sum_p A[prod_a[p]] . B[prod_b[p]]^T over K.  layout bit 0: A pieces
+ * are stored (K,M) instead of (M,K) (MN-major); bit 1: B pieces (K,N) instead of (N,K).
+ * Pieces are bf16, 16-byte aligned, row strides lda / ldb multiples of 8 elements; D fp32
+ * row stride ldd.  ksplit > 1 splits the reduction (partials in the workspace, summed in
+ * a fixed order); block_n = 64, 128 or 256 output columns per tile. */
+size_t delrec_tc_gemm_workspace(int M, int N, int ksplit);
+int delrec_tc_gemm(int M, int N, int K, int layout, int a_pieces, const void* const* A, long long lda,
+                   int b_pieces, const void* const* B, long long ldb, int nprod, const int* prod_a,
+                   const int* prod_b, int ksplit, int block_n, float* D, long long ldd, int accumulate,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
 /* Same as delrec_axonal_forward but allocation-free: no reference counterpart.  It is for
  * callers that cannot call cudaMalloc while the layer runs (all device memory handed to
  * their own allocator, no device-wide synchronisation allowed in the loop, or a plugin

@@ -17,6 +17,7 @@
 #include "backward_axonal_mma.cuh"
 #include "dense.cuh"
 #include "forward.cuh"
+#include "gemm_tc.cuh"
 #include "grads.cuh"
 #include "linear.cuh"
 #include "misc.cuh"
@@ -640,120 +641,113 @@ static int cublas_for_device(cublasHandle_t* out) {
 
 static int cublas_on(cublasHandle_t* h, void* cws, cudaStream_t st);
 
-// bytes of the tensor-core dW path: bf16 splits of gr (with nk-1 zero time rows appended)
-// and of each z variant, K+1 P matrices, the cuBLAS workspace
+static inline int pad8(int n) { return (n + 7) / 8 * 8; }
+// Split of the dW-type reductions (over the T*B rows) and its tile width.
+static int dw_bn(const delrec_layer* ly) { return gemm_pick_bn(ly->N); }
+static int dw_ksplit(const delrec_layer* ly, int nprod, int nslices) {
+  return gemm_pick_ksplit(ly->N, ly->N, ly->T * ly->B, nprod, 1, nslices, dw_bn(ly));
+}
+
+// bytes of the tensor-core dW path: bf16 pieces of gr and of each z variant, the
+// split-reduction partials, and (synaptic) the L lag products
 static size_t dense_dw_ws(const delrec_layer* ly, int nz, int nk) {
-  const size_t TBN = (size_t)ly->T * ly->B * ly->N, nn = (size_t)ly->N * ly->N;
-  const size_t pad = (size_t)(nk - 1) * ly->B * ly->N;
+  const size_t TBN = (size_t)ly->T * ly->B * pad8(ly->N), nn = (size_t)ly->N * ly->N;
   Carve c(nullptr, (size_t)-1);
-  c.take<__nv_bfloat16>((TBN + pad) * 2);
+  c.take<__nv_bfloat16>(TBN * 2);
   c.take<__nv_bfloat16>(TBN * 2 * nz);
-  if (nk > 1) c.take<float>(nn * nk);
-  c.take<unsigned char>(kCublasWs);
+  if (ly->kind == DELREC_SYNAPTIC) c.take<float>(nn * nk);
+  const int np = ly->kind == DELREC_SYNAPTIC ? 2 : 3;
+  c.take<unsigned char>(gemm_partial_bytes(ly->N, ly->N, dw_ksplit(ly, np, nk), nk));
   return c.off;
 }
 
-// Buffers of the tensor-core dW path (inside the caller's workspace).
+// Buffers of the tensor-core dW path (inside the caller's workspace).  The bf16 pieces
+// are (T*B, Np) with Np = N rounded up to 8 (16-byte rows for the tensor maps).
 struct DenseBufs {
-  __nv_bfloat16* g16;   // gr pieces: hi [GR], lo [GR]; GR = T*B*N + (nk-1)*B*N (zero tail)
-  __nv_bfloat16* z16;   // z variant v: hi at v*2*T*B*N, lo T*B*N after it
-  float* P;             // (nk, N, N) per-offset products, or dW itself when nk == 1
-  void* cws;            // cuBLAS workspace
-  size_t GR;
+  __nv_bfloat16* g16;   // gr pieces: hi [T*B*Np], lo [T*B*Np]
+  __nv_bfloat16* z16;   // z variant v: hi at v*2*T*B*Np, lo T*B*Np after it
+  float* P;             // synaptic: (L, N, N) lag products
+  float* part;          // split-reduction partials
 };
-static bool dense_carve(const delrec_layer* ly, int nz, int nk, float* dW, Carve& c, DenseBufs* d) {
-  const size_t TBN = (size_t)ly->T * ly->B * ly->N, nn = (size_t)ly->N * ly->N;
-  d->GR = TBN + (size_t)(nk - 1) * ly->B * ly->N;
-  d->g16 = c.take<__nv_bfloat16>(d->GR * 2);
+static bool dense_carve(const delrec_layer* ly, int nz, int nk, Carve& c, DenseBufs* d) {
+  const size_t TBN = (size_t)ly->T * ly->B * pad8(ly->N), nn = (size_t)ly->N * ly->N;
+  d->g16 = c.take<__nv_bfloat16>(TBN * 2);
   d->z16 = c.take<__nv_bfloat16>(TBN * 2 * nz);
-  d->P = nk > 1 ? c.take<float>(nn * nk) : dW;
-  d->cws = c.take<unsigned char>(kCublasWs);
+  d->P = ly->kind == DELREC_SYNAPTIC ? c.take<float>(nn * nk) : nullptr;
+  const int np = ly->kind == DELREC_SYNAPTIC ? 2 : 3;
+  d->part = (float*)c.take<unsigned char>(gemm_partial_bytes(ly->N, ly->N, dw_ksplit(ly, np, nk), nk));
   return c.ok;
 }
 
+// A (T*B, N) activation's bf16 pieces as an MN-major GEMM operand (reduced over T*B).
+static GemmSide rows_operand(const __nv_bfloat16* p0, const __nv_bfloat16* p1, int n, const delrec_layer* ly) {
+  GemmSide s{};
+  s.p[0] = p0;
+  s.p[1] = p1;
+  s.n = n;
+  s.rows = (long long)ly->T * ly->B;
+  s.cols = ly->N;
+  s.ld = pad8(ly->N);
+  s.mn_major = 1;
+  return s;
+}
+
 // dW (N,N) from gr (T,B,N) and the z variants (already in d.z16), v = min(k, nz-1) for
-// offset k.  P_k = sum_r Z_v(k)[r] (x) G[r + k*B] over the T*B rows r; the gr pieces carry
-// (nk-1)*B zero rows at the end, so every offset reads T*B rows and the offsets sharing
-// a z variant form one strided-batched GEMM (batch stride k*B*N on G, N*N on P).
+// offset k:  dW[i,o] = sum_r gr[r + k_io*B, i] z_v[r, o] over the T*B rows r, on the
+// tensor cores as three bf16 piece products (hi.hi + hi.lo + lo.hi) with the offset k as
+// the batch index (a row shift of the gr operand; rows past T*B read as zero) and each
+// batch writing only the synapses whose offset is k.
 static int dense_dw(const delrec_layer* ly, const float* gr, int nz, int nk, const uint8_t* offT, float* dW,
                     const DenseBufs& d, cudaStream_t st) {
   const int N = ly->N, T = ly->T, B = ly->B;
-  const size_t TBN = (size_t)T * B * N, nn = (size_t)N * N;
-  const size_t GR = d.GR;
-  k_split_bf16<<<grid_for(TBN, 256), 256, 0, st>>>(gr, TBN, d.g16, d.g16 + GR);
+  const size_t TBN = (size_t)T * B * pad8(N);
+  k_split_bf16_rows<<<grid_for(TBN, 256), 256, 0, st>>>(gr, (size_t)T * B, N, pad8(N), d.g16, d.g16 + TBN);
   DR_LAUNCHED();
-  if (GR > TBN) {
-    DR_CUDA(cudaMemsetAsync(d.g16 + TBN, 0, (GR - TBN) * sizeof(__nv_bfloat16), st));
-    DR_CUDA(cudaMemsetAsync(d.g16 + GR + TBN, 0, (GR - TBN) * sizeof(__nv_bfloat16), st));
-  }
-  cublasHandle_t h;
-  int rc = cublas_on(&h, d.cws, st);
-  if (rc) return rc;
-  const float one = 1.f, zero = 0.f;
-  const int rows = T * B;
+  const GemmSide A = rows_operand(d.g16, d.g16 + TBN, 2, ly);
+  const int BN = dw_bn(ly);
   // offsets k < nz-1 use z variant k alone; k >= nz-1 share variant nz-1 (one batch)
   for (int k0 = 0; k0 < nk;) {
     const int v = k0 < nz - 1 ? k0 : nz - 1;
     const int count = k0 < nz - 1 ? 1 : nk - k0;
     const __nv_bfloat16* Zh = d.z16 + (size_t)v * 2 * TBN;
-    const __nv_bfloat16* Zl = Zh + TBN;
-    const __nv_bfloat16* Gh = d.g16 + (size_t)k0 * B * N;
-    const __nv_bfloat16* Gl = d.g16 + GR + (size_t)k0 * B * N;
-    float* Pk = d.P + (size_t)k0 * nn;
-    // column-major view: C'(o,i) = sum_r Z'(o,r) G'(i,r)  ->  row-major P_k[i][o]
-    const __nv_bfloat16* As[3] = {Zh, Zh, Zl};
-    const __nv_bfloat16* Bs[3] = {Gh, Gl, Gh};
-    for (int p = 0; p < 3; ++p) {
-      const cublasStatus_t e = cublasGemmStridedBatchedEx(
-          h, CUBLAS_OP_N, CUBLAS_OP_T, N, N, rows, &one, As[p], CUDA_R_16BF, N, 0, Bs[p], CUDA_R_16BF, N,
-          (long long)B * N, p == 0 ? &zero : &one, Pk, CUDA_R_32F, N, (long long)nn, count, CUBLAS_COMPUTE_32F,
-          CUBLAS_GEMM_DEFAULT);
-      if (e != CUBLAS_STATUS_SUCCESS) {
-        fprintf(stderr, "delrec_b200: cublasGemmStridedBatchedEx failed (%d)\n", (int)e);
-        return DELREC_ERR_CUDA;
-      }
-    }
+    const GemmSide Bz = rows_operand(Zh, Zh + TBN, 2, ly);
+    GemmArgs g{};
+    g.M = N; g.N = N; g.K = T * B; g.nprod = 3; g.nseg = 1;
+    g.pa[0] = 0; g.pb[0] = 0; g.pa[1] = 0; g.pb[1] = 1; g.pa[2] = 1; g.pb[2] = 0;
+    g.a_k_z = B;            // offset k: gr rows shifted by k steps
+    g.z0 = k0;
+    g.ksplit = dw_ksplit(ly, 3, nk);
+    g.D = dW; g.ldd = N; g.d_z = 0;
+    g.mode = nk > 1 ? GEMM_MASKED : GEMM_STORE;
+    g.mask = offT; g.ldmask = 1; g.mask_cs = N;    // offT[o*N + i]: the offset of synapse (i, o)
+    const int rc = gemm_run(A, Bz, g, count, BN, d.part, st, &g_launches);
+    if (rc) return rc;
     k0 += count;
-  }
-  if (nk > 1) {
-    k_pick_by_offset<<<grid_for(nn, 256), 256, 0, st>>>(N, offT, d.P, dW);
-    DR_LAUNCHED();
   }
   return DELREC_OK;
 }
 
-// Synaptic layers: the per-lag correlation stack C_l = sum_r G[r + l*B] (x) Y[r] for all
-// lags l = 0..L-1 (the reference's Cstack), as two strided-batched bf16 GEMMs over the
-// T*B rows: gr split into hi + lo pieces, the spikes exact in one piece.  d.P receives C.
+// Synaptic layers: the per-lag correlation stack C_l = sum_r gr[r + l*B] (x) y[r] for all
+// lags l = 0..L-1 (the reference's Cstack), as one batched GEMM over the T*B rows: gr in
+// hi + lo pieces, the spikes exact in one piece, the lag as the batch index (a row shift
+// of the gr operand).  d.P receives C (L, N, N).
 static int syn_cstack(const delrec_layer* ly, const float* gr, const float* y, const DenseBufs& d, cudaStream_t st) {
   const int N = ly->N, T = ly->T, B = ly->B, nk = ly->L;
-  const size_t TBN = (size_t)T * B * N, nn = (size_t)N * N;
-  const size_t GR = d.GR;
-  k_split_bf16<<<grid_for(TBN, 256), 256, 0, st>>>(gr, TBN, d.g16, d.g16 + GR);
+  const size_t TBN = (size_t)T * B * pad8(N), nn = (size_t)N * N;
+  k_split_bf16_rows<<<grid_for(TBN, 256), 256, 0, st>>>(gr, (size_t)T * B, N, pad8(N), d.g16, d.g16 + TBN);
   DR_LAUNCHED();
-  if (GR > TBN) {
-    DR_CUDA(cudaMemsetAsync(d.g16 + TBN, 0, (GR - TBN) * sizeof(__nv_bfloat16), st));
-    DR_CUDA(cudaMemsetAsync(d.g16 + GR + TBN, 0, (GR - TBN) * sizeof(__nv_bfloat16), st));
-  }
-  k_split_bf16<<<grid_for(TBN, 256), 256, 0, st>>>(y, TBN, d.z16, d.z16 + TBN);   // 0/1: lo = 0
+  k_split_bf16_rows<<<grid_for(TBN, 256), 256, 0, st>>>(y, (size_t)T * B, N, pad8(N), d.z16, d.z16 + TBN);
   DR_LAUNCHED();
-  cublasHandle_t h;
-  int rc = cublas_on(&h, d.cws, st);
-  if (rc) return rc;
-  const float one = 1.f, zero = 0.f;
-  const __nv_bfloat16* Gs[2] = {d.g16, d.g16 + GR};
-  for (int p = 0; p < 2; ++p) {
-    // column-major view: C'(o,i) = sum_r Y'(o,r) G'(i,r + l*B)  ->  row-major C_l[i][o]
-    const cublasStatus_t e = cublasGemmStridedBatchedEx(
-        h, CUBLAS_OP_N, CUBLAS_OP_T, N, N, T * B, &one, d.z16, CUDA_R_16BF, N, 0, Gs[p], CUDA_R_16BF, N,
-        (long long)B * N, p == 0 ? &zero : &one, d.P, CUDA_R_32F, N, (long long)nn, nk, CUBLAS_COMPUTE_32F,
-        CUBLAS_GEMM_DEFAULT);
-    if (e != CUBLAS_STATUS_SUCCESS) {
-      fprintf(stderr, "delrec_b200: cublasGemmStridedBatchedEx failed (%d)\n", (int)e);
-      return DELREC_ERR_CUDA;
-    }
-  }
-  return DELREC_OK;
+  const GemmSide A = rows_operand(d.g16, d.g16 + TBN, 2, ly);
+  const GemmSide Y = rows_operand(d.z16, nullptr, 1, ly);
+  GemmArgs g{};
+  g.M = N; g.N = N; g.K = T * B; g.nprod = 2; g.nseg = 1;
+  g.pa[0] = 0; g.pb[0] = 0; g.pa[1] = 1; g.pb[1] = 0;
+  g.a_k_z = B;
+  g.ksplit = dw_ksplit(ly, 2, nk);
+  g.D = d.P; g.ldd = N; g.d_z = (long long)nn;
+  g.mode = GEMM_STORE;
+  return gemm_run(A, Y, g, nk, dw_bn(ly), d.part, st, &g_launches);
 }
 
 // ---- feedforward projection on tensor cores (linear.cuh) ------------------------
@@ -768,12 +762,44 @@ static LinPlan plan_linear(int K, int N, int x_binary) {
   p.nbx = x_binary ? 1 : 3;
   return p;
 }
+// K-major bf16 operand: rows x cols, row stride ld
+static GemmSide kmajor_operand(const void* p, long long rows, long long cols, long long ld) {
+  GemmSide s{};
+  s.p[0] = p;
+  s.n = 1;
+  s.rows = rows;
+  s.cols = cols;
+  s.ld = ld;
+  s.mn_major = 0;
+  return s;
+}
+// MN-major bf16 operand: krows (reduction) x cols, row stride ld
+static GemmSide mnmajor_operand(const void* p, long long krows, long long cols, long long ld) {
+  GemmSide s = kmajor_operand(p, krows, cols, ld);
+  s.mn_major = 1;
+  return s;
+}
+// one-product GEMM D (M x Nn) (mode) = A . B^T over K, split as gemm_pick_ksplit decides
+static int gemm1(const GemmSide& A, const GemmSide& B, int M, int Nn, int K, float* D, long long ldd, int mode,
+                 float* part, int max_ks, cudaStream_t st) {
+  GemmArgs g{};
+  g.M = M; g.N = Nn; g.K = K; g.nprod = 1; g.nseg = 1;
+  const int BN = gemm_pick_bn(Nn);
+  g.ksplit = gemm_pick_ksplit(M, Nn, K, 1, 1, 1, BN, max_ks);
+  g.D = D; g.ldd = ldd; g.mode = mode;
+  return gemm_run(A, B, g, 1, BN, part, st, &g_launches);
+}
+static size_t gemm1_part_bytes(int M, int Nn, int K, int max_ks) {
+  return gemm_partial_bytes(M, Nn, gemm_pick_ksplit(M, Nn, K, 1, 1, 1, gemm_pick_bn(Nn), max_ks), 1);
+}
+static constexpr int kLinMaxSplit = 8;
+
 static size_t linear_fwd_ws(int M, int K, int N, int xb) {
   const LinPlan p = plan_linear(K, N, xb);
   Carve c(nullptr, (size_t)-1);
   c.take<__nv_bfloat16>((size_t)M * p.pf * p.Kp);
   c.take<__nv_bfloat16>((size_t)N * p.pf * p.Kp);
-  c.take<unsigned char>(kCublasWs);
+  c.take<unsigned char>(gemm1_part_bytes(M, N, p.pf * p.Kp, kLinMaxSplit));
   return c.off;
 }
 static size_t linear_bwd_ws(int M, int K, int N, int xb) {
@@ -783,7 +809,8 @@ static size_t linear_bwd_ws(int M, int K, int N, int xb) {
   c.take<__nv_bfloat16>((size_t)M * 6 * p.Np);
   c.take<__nv_bfloat16>((size_t)6 * p.Np * p.Kp);
   c.take<float>((size_t)3 * p.Np * p.Kp);
-  c.take<unsigned char>(kCublasWs);
+  c.take<unsigned char>(std::max(gemm1_part_bytes(M, K, 6 * p.Np, kLinMaxSplit),
+                                 gemm1_part_bytes(3 * p.Np, p.Kp, M, kLinMaxSplit)));
   return c.off;
 }
 static int gemm_bf16(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k,
@@ -825,7 +852,7 @@ static int run_linear_forward(int M, int K, int N, const float* x, const float* 
   Carve c(ws, wsb);
   __nv_bfloat16* X = c.take<__nv_bfloat16>((size_t)M * p.pf * p.Kp);
   __nv_bfloat16* Wp = c.take<__nv_bfloat16>((size_t)N * p.pf * p.Kp);
-  void* cws = c.take<unsigned char>(kCublasWs);
+  float* part = (float*)c.take<unsigned char>(gemm1_part_bytes(M, N, p.pf * p.Kp, kLinMaxSplit));
   if (!c.ok) return DELREC_ERR_WORKSPACE;
   k_pack_rows<<<grid_for((size_t)M * p.Kp / 8, 256), 256, 0, st>>>(M, K, p.Kp, x, K, nullptr, 1, p.pf,
                                                                    xb ? kPatSpike3 : kPatReal6, xb, X);
@@ -833,12 +860,10 @@ static int run_linear_forward(int M, int K, int N, const float* x, const float* 
   k_pack_rows<<<grid_for((size_t)N * p.Kp / 8, 256), 256, 0, st>>>(N, K, p.Kp, W, K, bias, 0, p.pf,
                                                                    xb ? kPatW3 : kPatW6, 0, Wp);
   DR_LAUNCHED();
-  cublasHandle_t h;
-  int rc = cublas_on(&h, cws, st);
-  if (rc) return rc;
-  // column-major: out^T (N x M) = W'^T-view (N x P*Kp) . X'^T-view (P*Kp x M)
-  return gemm_bf16(h, CUBLAS_OP_T, CUBLAS_OP_N, N, M, p.pf * p.Kp, Wp, p.pf * p.Kp, X, p.pf * p.Kp, 0.f,
-                   out, N);
+  // out[m][n] = sum_c X'[m][c] W'[n][c]: the piece products laid along the reduction
+  const int Kt = p.pf * p.Kp;
+  return gemm1(kmajor_operand(X, M, Kt, Kt), kmajor_operand(Wp, N, Kt, Kt), M, N, Kt, out, N, GEMM_STORE, part,
+               kLinMaxSplit, st);
 }
 
 static int run_linear_backward(int M, int K, int N, const float* x, const float* W, const float* gout, int xb,
@@ -851,7 +876,8 @@ static int run_linear_backward(int M, int K, int N, const float* x, const float*
   __nv_bfloat16* G = c.take<__nv_bfloat16>((size_t)M * 6 * p.Np);
   __nv_bfloat16* Wt = c.take<__nv_bfloat16>((size_t)6 * p.Np * p.Kp);
   float* D = c.take<float>((size_t)3 * p.Np * p.Kp);
-  void* cws = c.take<unsigned char>(kCublasWs);
+  float* part = (float*)c.take<unsigned char>(std::max(gemm1_part_bytes(M, K, 6 * p.Np, kLinMaxSplit),
+                                                       gemm1_part_bytes(3 * p.Np, p.Kp, M, kLinMaxSplit)));
   if (!c.ok) return DELREC_ERR_WORKSPACE;
   // G' = [g0 g1 g2 g0 g1 g0]; the weight-gradient products read only its first three blocks,
   // so without dx the last three are not written (gb: blocks per row of G')
@@ -859,24 +885,23 @@ static int run_linear_backward(int M, int K, int N, const float* x, const float*
   k_pack_rows<<<grid_for((size_t)M * p.Np / 8, 256), 256, 0, st>>>(M, N, p.Np, gout, N, nullptr, 0, gb, kPatReal6,
                                                                    0, G);
   DR_LAUNCHED();
-  cublasHandle_t h;
-  int rc = cublas_on(&h, cws, st);
-  if (rc) return rc;
   if (dx) {
     k_pack_wt<<<grid_for((size_t)p.Np * p.Kp / 8, 256), 256, 0, st>>>(N, K, p.Np, p.Kp, W, kPatW6, 6, Wt);
     DR_LAUNCHED();
-    // column-major: dx^T (K x M) = W''-view (K x 6Np) . G'-view (6Np x M)
-    rc = gemm_bf16(h, CUBLAS_OP_N, CUBLAS_OP_N, K, M, 6 * p.Np, Wt, p.Kp, G, 6 * p.Np, 0.f, dx, K);
+    // dx[m][k] = sum_c G'[m][c] W''[c][k]  (W'' rows along the reduction: MN-major)
+    const int rc = gemm1(kmajor_operand(G, M, 6 * p.Np, 6 * p.Np), mnmajor_operand(Wt, 6 * p.Np, K, p.Kp), M, K,
+                         6 * p.Np, dx, K, GEMM_STORE, part, kLinMaxSplit, st);
     if (rc) return rc;
   }
   if (dW || dbias) {
     k_pack_rows<<<grid_for((size_t)M * p.Kp / 8, 256), 256, 0, st>>>(M, K, p.Kp, x, K, nullptr, 1, p.nbx,
                                                                      kPatDistinct3, xb, X);
     DR_LAUNCHED();
-    // column-major: D (Kp x 3Np) = sum_a X_a-view (Kp x M) . G'-view^T (M x (3-a)Np)
+    // D[c][k'] (+)= sum_m G'[m][c] X_a[m][k'] over the M rows, c < (3-a) Np
     for (int a = 0; a < p.nbx; ++a) {
-      rc = gemm_bf16(h, CUBLAS_OP_N, CUBLAS_OP_T, p.Kp, (3 - a) * p.Np, M, X + (size_t)a * p.Kp, p.nbx * p.Kp, G,
-                     gb * p.Np, a == 0 ? 0.f : 1.f, D, p.Kp);
+      const int rc = gemm1(mnmajor_operand(G, M, (long long)(3 - a) * p.Np, (long long)gb * p.Np),
+                           mnmajor_operand(X + (size_t)a * p.Kp, M, p.Kp, (long long)p.nbx * p.Kp), (3 - a) * p.Np,
+                           p.Kp, M, D, p.Kp, a == 0 ? GEMM_STORE : GEMM_ACCUM, part, kLinMaxSplit, st);
       if (rc) return rc;
     }
     k_linear_dw_reduce<<<grid_for((size_t)N * (K + 1), 256), 256, 0, st>>>(N, K, p.Np, p.Kp, D, dW, dbias);
@@ -888,15 +913,17 @@ static int run_linear_backward(int M, int K, int N, const float* x, const float*
 // Axonal layers too wide for the single-wave scans run step by step: per reverse step one
 // LIF-backward kernel and one bf16 GEMM gz(t) = [hi hi lo](gr(t)) . [W_hi; W_lo; W_hi].
 static bool plan_axstep(const delrec_layer* ly, const BwdPlan& bp, bool single_wave_ok) {
-  return ly->kind == DELREC_AXONAL && !single_wave_ok && ly->N > 512 && bp.MM == 0;
+  // (the per-step GEMM's operands need 16-byte rows: N a multiple of 8)
+  return ly->kind == DELREC_AXONAL && !single_wave_ok && ly->N > 512 && bp.MM == 0 && ly->N % 8 == 0;
 }
+static constexpr int kStepMaxSplit = 2;
 static size_t axstep_ws(const delrec_layer* ly) {
   const size_t N = ly->N, BN = (size_t)ly->B * N;
   Carve c(nullptr, (size_t)-1);
   c.take<float>(BN);                          // lam
   c.take<__nv_bfloat16>(3 * N * N);           // [W_hi; W_lo; W_hi]
   c.take<__nv_bfloat16>(3 * BN);              // [hi | hi | lo] of gr(t)
-  c.take<unsigned char>(kCublasWs);
+  c.take<unsigned char>(gemm1_part_bytes(ly->B, ly->N, 3 * ly->N, kStepMaxSplit));
   return c.off;
 }
 static int run_axstep(const delrec_layer* ly, const delrec_lif* lif, const float* gy, const float* u,
@@ -907,23 +934,22 @@ static int run_axstep(const delrec_layer* ly, const delrec_lif* lif, const float
   float* lam = c.take<float>(BN);
   __nv_bfloat16* Wp = c.take<__nv_bfloat16>(3 * nn);
   __nv_bfloat16* g3 = c.take<__nv_bfloat16>(3 * BN);
-  void* cws = c.take<unsigned char>(kCublasWs);
+  float* part = (float*)c.take<unsigned char>(gemm1_part_bytes(B, N, 3 * N, kStepMaxSplit));
   if (!c.ok) return DELREC_ERR_WORKSPACE;
   DR_CUDA(cudaMemsetAsync(lam, 0, BN * sizeof(float), st));
   k_split_bf16<<<grid_for(nn, 256), 256, 0, st>>>(W, nn, Wp, Wp + nn);
   DR_LAUNCHED();
   DR_CUDA(cudaMemcpyAsync(Wp + 2 * nn, Wp, nn * sizeof(__nv_bfloat16), cudaMemcpyDeviceToDevice, st));
-  cublasHandle_t h;
-  int rc = cublas_on(&h, cws, st);
-  if (rc) return rc;
   const LifK lk = make_lif(*lif);
+  // gz(t)[b][o] = sum_c g3[b][c] Wp[c][o], c over the 3N piece rows (W rows: MN-major operand)
+  const GemmSide A = kmajor_operand(g3, B, 3 * N, 3 * N);
+  const GemmSide Wm = mnmajor_operand(Wp, 3 * N, N, N);
   scan_mark(0, st);
   for (int t = T - 1; t >= 0; --t) {
     k_step_lif_bwd<<<grid_for(BN, 256), 256, 0, st>>>(t, T, B, N, TAPS, gy, u, keep, tl0, tnt, tw, gz, lam, dx,
                                                       gr, g3, lk);
     DR_LAUNCHED();
-    // column-major: gz(t)^T (N x B) = [W_hi; W_lo; W_hi]-view (N x 3N) . g3-view (3N x B)
-    rc = gemm_bf16(h, CUBLAS_OP_N, CUBLAS_OP_N, N, B, 3 * N, Wp, N, g3, 3 * N, 0.f, gz + (size_t)t * BN, N);
+    const int rc = gemm1(A, Wm, B, N, 3 * N, gz + (size_t)t * BN, N, GEMM_STORE, part, kStepMaxSplit, st);
     if (rc) return rc;
   }
   scan_mark(1, st);
@@ -1137,7 +1163,7 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
   SrcArgs sa{};
   sa.T = T; sa.B = B; sa.N = N; sa.TAPS = bp.TAPS;
   sa.gr = gr; sa.gz = kind != DELREC_SYNAPTIC ? gz : nullptr; sa.y = y; sa.tap_l0 = tl0; sa.tap_nt = tnt;
-  sa.tap_w = tw; sa.part = spart; sa.MM = bp.MM;
+  sa.tap_w = tw; sa.part = spart; sa.MM = bp.MM; sa.Np = pad8(N);
   const dim3 sgrid(cdiv(N, 32), cdiv(B, 8), sp.tsplit);
   if (kind != DELREC_SYNAPTIC) {
     // one pass over (gr, y, gz at spikes) -> db/dmask partials and the bf16 z pieces of
@@ -1148,7 +1174,10 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
       const size_t dws = dense_dw_ws(ly, nz, nk);
       unsigned char* region = c.take<unsigned char>(dws);
       Carve dc(region, dws);
-      if (!dense_carve(ly, nz, nk, g->dW, dc, &dbf)) return DELREC_ERR_WORKSPACE;
+      if (!dense_carve(ly, nz, nk, dc, &dbf)) return DELREC_ERR_WORKSPACE;
+      // the source pass writes columns < N of the z pieces; the row padding stays zero
+      if (pad8(N) != N)
+        DR_CUDA(cudaMemsetAsync(dbf.z16, 0, (size_t)T * B * pad8(N) * 2 * nz * sizeof(__nv_bfloat16), st));
     }
     if (g->dW || need_src) {
       const int wz = g->dW ? 1 : 0, warm = ly->L - 1 + bp.MM;
@@ -1176,7 +1205,7 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
       unsigned char* region = c.take<unsigned char>(dws);
       Carve dc(region, dws);
       DenseBufs dbf{};
-      if (!c.ok || !dense_carve(ly, 1, nk, nullptr, dc, &dbf)) return DELREC_ERR_WORKSPACE;
+      if (!c.ok || !dense_carve(ly, 1, nk, dc, &dbf)) return DELREC_ERR_WORKSPACE;
       rc = syn_cstack(ly, gr, y, dbf, st);
       if (rc) return rc;
       const size_t nn = (size_t)N * N;
@@ -1410,6 +1439,35 @@ int delrec_dcls_backward(int T, int B, int Cin, int Cout, int groups, int K, int
     DR_LAUNCHED();
   }
   return DELREC_OK;
+}
+
+// ---- the library's tensor-core GEMM, exposed for testing and for callers' own use ----
+size_t delrec_tc_gemm_workspace(int M, int N, int ksplit) {
+  return (M > 0 && N > 0 && ksplit > 0) ? gemm_partial_bytes(M, N, ksplit, 1) : 0;
+}
+
+int delrec_tc_gemm(int M, int N, int K, int layout, int a_pieces, const void* const* A, long long lda,
+                   int b_pieces, const void* const* B, long long ldb, int nprod, const int* prod_a,
+                   const int* prod_b, int ksplit, int block_n, float* D, long long ldd, int accumulate, void* ws,
+                   size_t wsb, void* stream) {
+  if (M < 1 || N < 1 || K < 1 || !A || !B || !D || !prod_a || !prod_b) return DELREC_ERR_ARG;
+  if (a_pieces < 1 || a_pieces > 3 || b_pieces < 1 || b_pieces > 3 || nprod < 1 || nprod > kGemmMaxProd)
+    return DELREC_ERR_ARG;
+  if (ksplit < 1 || ldd < N) return DELREC_ERR_ARG;
+  if (ksplit > 1 && (((uintptr_t)ws & 255) != 0 || wsb < gemm_partial_bytes(M, N, ksplit, 1)))
+    return DELREC_ERR_WORKSPACE;
+  GemmSide as{}, bs{};
+  as.n = a_pieces; as.ld = lda; as.mn_major = (layout & 1) ? 1 : 0;
+  as.rows = as.mn_major ? K : M; as.cols = as.mn_major ? M : K;
+  bs.n = b_pieces; bs.ld = ldb; bs.mn_major = (layout & 2) ? 1 : 0;
+  bs.rows = bs.mn_major ? K : N; bs.cols = bs.mn_major ? N : K;
+  for (int i = 0; i < a_pieces; ++i) as.p[i] = A[i];
+  for (int i = 0; i < b_pieces; ++i) bs.p[i] = B[i];
+  GemmArgs g{};
+  g.M = M; g.N = N; g.K = K; g.nprod = nprod; g.nseg = 1; g.ksplit = ksplit;
+  for (int p = 0; p < nprod; ++p) { g.pa[p] = prod_a[p]; g.pb[p] = prod_b[p]; }
+  g.D = D; g.ldd = ldd; g.mode = accumulate ? GEMM_ACCUM : GEMM_STORE;
+  return gemm_run(as, bs, g, 1, block_n, (float*)ws, (cudaStream_t)stream, &g_launches);
 }
 
 // ---- allocation-free variant of the axonal forward --------------------------------

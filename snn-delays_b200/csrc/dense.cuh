@@ -26,6 +26,21 @@ __global__ void k_split_bf16(const float* __restrict__ x, size_t n, __nv_bfloat1
   }
 }
 
+// hi + lo bf16 pieces of a (rows, N) fp32 matrix written with row stride Np >= N (the
+// GEMM operand layout; columns N..Np-1 are zero)
+__global__ void k_split_bf16_rows(const float* __restrict__ x, size_t rows, int N, int Np,
+                                  __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
+  const size_t total = rows * (size_t)Np;
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = e / Np;
+    const int n = (int)(e % Np);
+    const float v = n < N ? x[r * N + n] : 0.f;
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    hi[e] = h;
+    lo[e] = __float2bfloat16_rn(v - __bfloat162float(h));
+  }
+}
+
 // One reverse step of an axonal layer run step by step (layers too wide for the
 // single-wave scans): for every (b, o),
 //   gfut = sum_j w_o[j] gz(t + l_j)[b, o]  (gz of later steps, from the per-step GEMMs),

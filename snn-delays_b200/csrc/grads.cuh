@@ -83,6 +83,7 @@ struct SrcArgs {
   const int* tap_nt;
   const float* tap_w;   // k_source_pass: the taps' weights (z pieces)
   float* part;
+  int Np;               // k_source_pass: row stride of the z pieces (N rounded up to 8)
 };
 
 template <int TAPSMAX>
@@ -207,6 +208,7 @@ __global__ void __launch_bounds__(256, 2) k_source_pass(SrcArgs a, int want_z, i
   if (n < N && b < B && c0 < c1) {
     const size_t step = (size_t)B * N;
     const size_t TBN = (size_t)T * step;
+    const size_t ZP = (size_t)T * B * a.Np;   // one z piece (T*B rows of Np)
     const size_t base = (size_t)b * N + n;
     uint64_t h0 = 0ull, h1 = 0ull;
     // warm-up: spikes of the steps before the chunk (8 independent loads per batch)
@@ -244,13 +246,13 @@ __global__ void __launch_bounds__(256, 2) k_source_pass(SrcArgs a, int want_z, i
         h0 = (h0 << 1) | (yv[q] != 0.f ? 1ull : 0ull);
         // bit j: spike at te - l_j  (history bit l_j + MM); spikes before t=0 read as 0
         const uint32_t bits = hist_window(h0, h1, lo + MM) & tmask;
-        const size_t idx = (size_t)te * step + base;
+        const size_t zidx = ((size_t)te * B + b) * a.Np + n;
         if (bits == 0u) {
           if (want_z) {
             const __nv_bfloat16 zero = __float2bfloat16_rn(0.f);
             for (int m = 0; m <= MM; ++m) {
-              zh[(size_t)m * 2 * TBN + idx] = zero;
-              zh[(size_t)m * 2 * TBN + TBN + idx] = zero;
+              zh[(size_t)m * 2 * ZP + zidx] = zero;
+              zh[(size_t)m * 2 * ZP + ZP + zidx] = zero;
             }
           }
           continue;
@@ -275,8 +277,8 @@ __global__ void __launch_bounds__(256, 2) k_source_pass(SrcArgs a, int want_z, i
             for (int j = 0; j < TAPSMAX; ++j)
               if ((zb >> j) & 1u) acc = __fadd_rn(acc, tw[j]);
             const __nv_bfloat16 h = __float2bfloat16_rn(acc);
-            zh[(size_t)m * 2 * TBN + idx] = h;
-            zh[(size_t)m * 2 * TBN + TBN + idx] = __float2bfloat16_rn(acc - __bfloat162float(h));
+            zh[(size_t)m * 2 * ZP + zidx] = h;
+            zh[(size_t)m * 2 * ZP + ZP + zidx] = __float2bfloat16_rn(acc - __bfloat162float(h));
           }
         }
       }

@@ -73,6 +73,9 @@ _SIGS = {
     "delrec_linear_backward_workspace": (_S, [_I, _I, _I, _I]),
     "delrec_linear_backward": (_I, [_I, _I, _I, _P, _P, _P, _I, _P, _P, _P, _P, _S, _P]),
     "delrec_count_nonbinary": (_I, [_P, _S, _P, _P]),
+    "delrec_tc_gemm_workspace": (_S, [_I, _I, _I]),
+    "delrec_tc_gemm": (_I, [_I, _I, _I, _I, _I, _P, ctypes.c_longlong, _I, _P, ctypes.c_longlong, _I, _P, _P, _I, _I,
+                            _P, ctypes.c_longlong, _I, _P, _S, _P]),
     "delrec_get_status": (_I, [_P]),
     "delrec_clear_status": (_I, []),
     "delrec_version": (ctypes.c_char_p, []),
