@@ -6,9 +6,11 @@
  * source neuron o): rec[b,i] = sum_o W[i,o] * (delayed spike of o).
  * Every entry point launches on `stream` (a cudaStream_t; NULL = legacy default stream)
  * and returns DELREC_OK or an error code.  Scratch memory is passed in by the caller:
- * query its size with the matching *_workspace function.  The axonal and hybrid
- * backward run their weight-gradient GEMMs through cuBLAS (on a slice of that
- * workspace); the cuBLAS handle is created on the first such call on each device.
+ * query its size with the matching *_workspace function.  Weight gradients, the
+ * synaptic lag stack, the projections and the chunked reverse scan run on the library's
+ * own tcgen05 GEMM; only the step-by-step forward of axonal layers wider than 512 neurons
+ * calls cuBLAS (one IEEE fp32 GEMM per step, on a slice of the workspace; the handle is
+ * created on the first such call on each device).
  *
  * Reference interfaces replaced (paths are inside ZiyadBekrar/SNN-delays):
  *   delrec_build_mask             triton_kernels/delays.py:13-29, 48-63 (build_mask,
@@ -176,6 +178,10 @@ int delrec_hybrid_forward(const delrec_layer* layer, const delrec_lif* lif,
                           const float* base, const float* offsets, const float* s,
                           const float* keep, float* y, float* u,
                           void* workspace, size_t workspace_bytes, void* stream);
+/* The backward factors each synapse's delay into base + offset and supports base tap
+ * windows that reach at most one lag below lag 1 (layer->d_min, s_max); a wider window
+ * returns DELREC_ERR_UNSUPPORTED -- run such a layer through delrec_synaptic_* on the
+ * materialised delay d[i,o] = base[o] + offsets[i,o] (the Python Function does). */
 size_t delrec_hybrid_backward_workspace(const delrec_layer* layer);
 int delrec_hybrid_backward(const delrec_layer* layer, const delrec_lif* lif,
                            const float* gy, const float* u, const float* y,
@@ -216,8 +222,8 @@ int delrec_dcls_backward(int T, int B, int Cin, int Cout, int groups, int K, int
  * Runs on bf16 tensor cores with fp32 accuracy: each fp32 operand is split exactly into
  * three bf16 pieces and the piece products with i + j <= 2 are summed with fp32
  * accumulation.  x_binary = 1 promises x in {0, 1} (spike trains: three products instead
- * of six); a violated promise sets the status word.  The GEMMs run through cuBLAS on a
- * slice of the workspace. */
+ * of six); a violated promise sets the status word.  The GEMMs run on the library's
+ * tcgen05 GEMM (partials on a slice of the workspace). */
 size_t delrec_linear_forward_workspace(int M, int K, int N, int x_binary);
 int delrec_linear_forward(int M, int K, int N, const float* x, const float* W, const float* bias,
                           int x_binary, float* out, void* workspace, size_t workspace_bytes,
@@ -247,6 +253,14 @@ unsigned long long delrec_launch_count(void);
  * returns the summed milliseconds and the number of launches since enabling. */
 int delrec_scan_timing(int enable);
 int delrec_scan_time(double* total_ms, int* launches);
+/* Reverse-scan variant of the layer backwards (process-wide).  0 (default): hybrid layers
+ * whose shape allows it run the chunked scan -- the delayed-gradient contraction of every
+ * synapse whose lag reaches past the current 8-step chunk as one tensor-core GEMM per
+ * chunk, the short-lag synapses step by step; 1: the step-by-step scans only.  Both give
+ * the reference's gradients within the library's tolerance; the workspace size queries
+ * cover either variant.  Replaces no reference call (the reference has one Triton
+ * kernel per layer kind, triton_kernels/synaptic_eventdriven.py:323-364). */
+int delrec_set_reverse_scan(int variant);
 
 #ifdef __cplusplus
 }

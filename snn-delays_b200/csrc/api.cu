@@ -15,6 +15,7 @@
 #include "backward_hybrid.cuh"
 #include "backward_hybrid64.cuh"
 #include "backward_axonal_mma.cuh"
+#include "backward_chunk.cuh"
 #include "dense.cuh"
 #include "forward.cuh"
 #include "gemm_tc.cuh"
@@ -110,7 +111,11 @@ static int hybrid_mm(const delrec_layer* ly) {
   if (mm > ly->K) mm = ly->K;
   return mm;
 }
-static constexpr int kMMMax = 3;
+// The factored hybrid backward keeps gz_m(tau) = sum_{k >= m} W_k gr(tau + k) for tau >= 0
+// only.  A base tap at lag l = 1 - m <= -1 needs gz_m(t + l) at t + l < 0 for the first
+// steps (t < m - 1), so layers whose base reaches two or more lags below lag 1 (MM >= 2)
+// take the per-synapse path on the materialised delay instead.
+static constexpr int kMMMax = 1;
 
 // --------------------------------------------------------------------------------
 // forward planning
@@ -956,6 +961,133 @@ static int run_axstep(const delrec_layer* ly, const delrec_lif* lif, const float
   return DELREC_OK;
 }
 
+// ---- chunked reverse scan (backward_chunk.cuh) ----------------------------------------
+// 0: hybrid layers run the chunked scan where the shape allows it; 1: every layer runs the
+// step-by-step scans (delrec_set_reverse_scan).
+static std::atomic<int> g_reverse_scan{0};
+
+struct ChunkPlan {
+  bool ok;
+  int KP1, ntiles, nchunks, Np;
+  size_t smem;
+};
+// Shape test only (the workspace query does not depend on the selected variant): a
+// hybrid layer that the 64-sample scan takes, offsets within two chunks (K + 1 <= 9).
+static ChunkPlan plan_chunk(const delrec_layer* ly, const BwdPlan& bp, const Hyb64Plan& h64) {
+  ChunkPlan c{};
+  c.ok = false;
+  if (!h64.ok || ly->kind != DELREC_HYBRID) return c;
+  c.KP1 = h64.K + 1;
+  if (c.KP1 > kChunk + 1 || bp.TAPS > kH64Taps) return c;
+  c.ntiles = cdiv(ly->N, kGzCols / c.KP1);
+  c.nchunks = cdiv(ly->T, kChunk);
+  c.Np = pad8(ly->N);
+  c.smem = hyb64_smem_plan(ly->N, h64.NT, h64.CAPS, h64.K, bp.TAPS, kChunk).total;
+  c.ok = c.smem <= kSmemLimit;
+  return c;
+}
+static size_t chunk_ws(const delrec_layer* ly, const ChunkPlan& cp) {
+  Carve c(nullptr, (size_t)-1);
+  const size_t rows = (size_t)ly->B * ly->T;
+  c.take<__nv_bfloat16>(rows * cp.Np);                       // gr pieces (B, T, Np)
+  c.take<__nv_bfloat16>(rows * cp.Np);
+  c.take<__nv_bfloat16>((size_t)cp.ntiles * kGzCols * cp.Np);   // masked W pieces
+  c.take<__nv_bfloat16>((size_t)cp.ntiles * kGzCols * cp.Np);
+  c.take<float>((size_t)ly->B * ly->N);                       // LIF carry between chunks
+  return c.off;
+}
+
+// (B, T, N) bf16 pieces read as boxes of 64 targets x 8 steps x 16 samples
+static bool tmap_bf16_btn(CUtensorMap* m, const void* base, int N, int T, int B, int Np) {
+  TmapEncodeFn fn = tmap_encoder();
+  if (!fn || !base || ((uintptr_t)base & 15) || (Np % 8)) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)T, (cuuint64_t)B};
+  const cuuint64_t strides[2] = {(cuuint64_t)Np * 2, (cuuint64_t)T * Np * 2};
+  const cuuint32_t box[3] = {64, (cuuint32_t)kChunk, (cuuint32_t)kGzSamples};
+  const cuuint32_t es[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int KP1>
+static int launch_gz_t(const CUtensorMap* m, const GzArgs& g, int ntiles, cudaStream_t st) {
+  auto kern = k_chunk_gz<KP1>;
+  int rc = set_smem(kern, kGzSmem);
+  if (rc) return rc;
+  kern<<<dim3(cdiv(g.B, kGzSamples), ntiles), 128, kGzSmem, st>>>(m[0], m[1], m[2], m[3], g);
+  DR_LAUNCHED();
+  return DELREC_OK;
+}
+static int launch_gz(int KP1, const CUtensorMap* m, const GzArgs& g, int ntiles, cudaStream_t st) {
+  switch (KP1) {
+    case 1: return launch_gz_t<1>(m, g, ntiles, st);
+    case 2: return launch_gz_t<2>(m, g, ntiles, st);
+    case 3: return launch_gz_t<3>(m, g, ntiles, st);
+    case 4: return launch_gz_t<4>(m, g, ntiles, st);
+    case 5: return launch_gz_t<5>(m, g, ntiles, st);
+    case 6: return launch_gz_t<6>(m, g, ntiles, st);
+    case 7: return launch_gz_t<7>(m, g, ntiles, st);
+    case 8: return launch_gz_t<8>(m, g, ntiles, st);
+    case 9: return launch_gz_t<9>(m, g, ntiles, st);
+    default: return DELREC_ERR_UNSUPPORTED;
+  }
+}
+
+// The chunked reverse scan of one layer: for each chunk of 8 steps, from the last, the
+// SIMT steps (k_bwd_chunk) and the tensor-core delayed-gradient GEMM (k_chunk_gz).
+// `base` carries the 64-sample scan's arguments (taps, buckets, exchange buffers).
+static int run_chunked(const delrec_layer* ly, const Hyb64Plan& h64, const ChunkPlan& cp, const Hyb64Args& base,
+                       const float* W, const uint8_t* offT, float* gz, Carve& c, cudaStream_t st) {
+  const int N = ly->N, T = ly->T, B = ly->B, Np = cp.Np;
+  const size_t rows = (size_t)B * T, wrows = (size_t)cp.ntiles * kGzCols;
+  __nv_bfloat16* ga_hi = c.take<__nv_bfloat16>(rows * Np);
+  __nv_bfloat16* ga_lo = c.take<__nv_bfloat16>(rows * Np);
+  __nv_bfloat16* wm_hi = c.take<__nv_bfloat16>(wrows * Np);
+  __nv_bfloat16* wm_lo = c.take<__nv_bfloat16>(wrows * Np);
+  float* lam = c.take<float>((size_t)B * N);
+  if (!c.ok) return DELREC_ERR_WORKSPACE;
+  k_mask_w<<<grid_for(wrows * Np, 256), 256, 0, st>>>(N, Np, cp.KP1, (int)wrows, W, offT, wm_hi, wm_lo);
+  DR_LAUNCHED();
+  DR_CUDA(cudaMemsetAsync(gz, 0, (size_t)T * B * N * sizeof(float), st));
+  CUtensorMap maps[4];
+  if (!tmap_bf16_btn(&maps[0], ga_hi, N, T, B, Np) || !tmap_bf16_btn(&maps[1], ga_lo, N, T, B, Np) ||
+      !tmap_bf16(&maps[2], wm_hi, N, (long long)wrows, Np, kGzCols) ||
+      !tmap_bf16(&maps[3], wm_lo, N, (long long)wrows, Np, kGzCols))
+    return DELREC_ERR_ARG;
+  auto kern = k_bwd_chunk<kH64Taps>;
+  int rc = set_smem(kern, cp.smem);
+  if (rc) return rc;
+  int per_sm = 0;
+  DR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kH64Threads, cp.smem));
+  if (per_sm < 1 || h64.CS * h64.tiles > per_sm * kSMs) return DELREC_ERR_UNSUPPORTED;
+  ChunkArgs a{};
+  a.T = T; a.B = B; a.N = N; a.K = h64.K; a.CS = h64.CS; a.NT = h64.NT; a.TAPS = base.TAPS;
+  a.CAPS = h64.CAPS; a.CAP = h64.CAP; a.boff_stride = base.boff_stride;
+  a.gy = base.gy; a.u = base.u; a.keep = base.keep;
+  a.tap_l0 = base.tap_l0; a.tap_nt = base.tap_nt; a.tap_w = base.tap_w; a.ent = base.ent; a.boff = base.boff;
+  a.dx = base.dx; a.gr = base.gr; a.gz = gz; a.ga_hi = ga_hi; a.ga_lo = ga_lo; a.Np = Np; a.lam = lam;
+  a.lif = base.lif; a.grx = base.grx; a.arrive = base.arrive; a.spin_limit = base.spin_limit;
+  GzArgs g{};
+  g.T = T; g.B = B; g.N = N; g.gz = gz; g.spin_ns = 2000000000ll;
+  scan_mark(0, st);
+  for (int ch = cp.nchunks - 1; ch >= 0; --ch) {
+    a.t0 = ch * kChunk;
+    a.t_hi = std::min(T - 1, a.t0 + kChunk - 1);
+    DR_CUDA(cudaMemsetAsync(a.arrive, 0, sizeof(unsigned int) * h64.tiles, st));
+    ChunkArgs ac = a;
+    void* args[] = {(void*)&ac};
+    DR_CUDA(cudaLaunchCooperativeKernel((const void*)kern, dim3(h64.CS * h64.tiles), dim3(kH64Threads), args,
+                                        cp.smem, st));
+    ++g_launches;
+    g.t0 = a.t0;
+    rc = launch_gz(cp.KP1, maps, g, cp.ntiles, st);
+    if (rc) return rc;
+  }
+  scan_mark(1, st);
+  return DELREC_OK;
+}
+
 static size_t backward_ws(const delrec_layer* ly, int kind) {
   const BwdPlan bp = plan_backward(ly, kind);
   const SrcPlan sp = plan_src(ly);
@@ -985,6 +1117,10 @@ static size_t backward_ws(const delrec_layer* ly, int kind) {
     }
   }
   if (plan_axstep(ly, bp, plan_axmma(ly, bp).ok || plan_hybrid64(ly, bp).ok)) c.take<unsigned char>(axstep_ws(ly));
+  if (kind == DELREC_HYBRID) {
+    const ChunkPlan cp = plan_chunk(ly, bp, plan_hybrid64(ly, bp));
+    if (cp.ok) c.take<unsigned char>(chunk_ws(ly, cp));
+  }
   if (kind == DELREC_AXONAL && plan_axmma(ly, bp).ok) {
     const AxMmaPlan am = plan_axmma(ly, bp);
     c.take<float>((size_t)2 * am.tiles * N * 64);
@@ -1133,6 +1269,7 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
     h.grx = grx; h.arrive = arrive; h.spin_limit = 1ll << 22;
     rc = launch_hyb64_t<kSynKmax>(h, s64, st);
   } else if (h64.ok) {
+    const ChunkPlan cp = plan_chunk(ly, bp, h64);
     Hyb64Args h{};
     h.T = T; h.B = B; h.N = N; h.K = h64.K; h.CS = h64.CS; h.NT = h64.NT; h.TAPS = bp.TAPS; h.CAPS = h64.CAPS;
     h.CAP = h64.CAP; h.boff_stride = h64.K + 2;
@@ -1140,7 +1277,14 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
     h.tap_l0 = tl0; h.tap_nt = tnt; h.tap_w = tw; h.ent = ent; h.boff = boff;
     h.dx = g->dx; h.gr = gr; h.gz = gz; h.lif = a.lif;
     h.grx = grx; h.arrive = arrive; h.spin_limit = 1ll << 22;
-    rc = h64.KMAX == 6 ? launch_hyb64_t<6>(h, h64, st) : launch_hyb64_t<10>(h, h64, st);
+    if (cp.ok && g_reverse_scan.load() == 0) {
+      const size_t cws = chunk_ws(ly, cp);
+      unsigned char* region = c.take<unsigned char>(cws);
+      Carve cc(region, cws);
+      rc = c.ok ? run_chunked(ly, h64, cp, h, W, offT, gz, cc, st) : DELREC_ERR_WORKSPACE;
+    } else {
+      rc = h64.KMAX == 6 ? launch_hyb64_t<6>(h, h64, st) : launch_hyb64_t<10>(h, h64, st);
+    }
   } else if (hp.ok) {
     HybArgs h{};
     h.grx = grx; h.arrive = arrive; h.spin_limit = 1ll << 22;
@@ -1268,6 +1412,12 @@ int delrec_scan_time(double* total_ms, int* launches) {
   *total_ms = sum;
   *launches = g_ev_n;
   g_ev_n = 0;
+  return DELREC_OK;
+}
+
+int delrec_set_reverse_scan(int variant) {
+  if (variant != 0 && variant != 1) return DELREC_ERR_ARG;
+  g_reverse_scan.store(variant);
   return DELREC_OK;
 }
 

@@ -82,6 +82,7 @@ _SIGS = {
     "delrec_launch_count": (ctypes.c_ulonglong, []),
     "delrec_scan_timing": (_I, [_I]),
     "delrec_scan_time": (_I, [_P, _P]),
+    "delrec_set_reverse_scan": (_I, [_I]),
 }
 
 _lib = None
@@ -173,6 +174,16 @@ def scan_time():
     n = ctypes.c_int(0)
     check(lib().delrec_scan_time(ctypes.byref(ms), ctypes.byref(n)), "delrec_scan_time")
     return ms.value, n.value
+
+
+REVERSE_SCAN_CHUNKED, REVERSE_SCAN_STEPWISE = 0, 1
+
+
+def set_reverse_scan(variant: int):
+    """Select the layer backwards' reverse scan for this process: REVERSE_SCAN_CHUNKED
+    (default: hybrid layers contract their long-lag synapses once per 8-step chunk on the
+    tensor cores) or REVERSE_SCAN_STEPWISE (the step-by-step scans only)."""
+    check(lib().delrec_set_reverse_scan(int(variant)), "delrec_set_reverse_scan")
 
 
 def status() -> int:

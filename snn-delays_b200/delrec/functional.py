@@ -65,7 +65,9 @@ def _layer(kind, T, B, N, L, K, has_bias, has_keep, s_max, d_min=0.0):
     return _lib.Layer(kind, T, B, N, L, K, int(has_bias), int(has_keep), float(s_max), float(d_min))
 
 
-HYBRID_MM_MAX = 3
+# The library's factored hybrid backward takes base windows reaching at most one lag below
+# lag 1; wider ones (bases near or below zero with a wide triangle) run the per-synapse path.
+HYBRID_MM_MAX = 1
 
 
 def hybrid_thresholds(base_min, s_max, K):

@@ -89,6 +89,10 @@ SHAPES = [
     ("synaptic", 25, 100, 96, 1.0, True, False, False, 12.0, 0),
     ("hybrid", 30, 100, 200, 0.0, False, True, True, 20.0, 8),
     ("hybrid", 24, 70, 512, 0.0, False, False, False, 3.0, 2),
+    # chunked reverse scan: a single partial chunk with wide taps (sigma > 0) and dropout;
+    # per-source widths, a ragged neuron slice and short base lags
+    ("hybrid", 7, 64, 256, 1.5, False, True, True, 12.0, 6),
+    ("hybrid", 33, 96, 300, 0.7, True, False, False, 6.0, 3),
 ]
 
 
@@ -103,17 +107,40 @@ def test_random_vs_oracle(shape):
     print(rec)
 
 
+@pytest.mark.parametrize("T,B,N,K,sigma", [(64, 256, 512, 8, 0.0), (45, 130, 264, 5, 1.0), (16, 40, 96, 8, 0.0)])
+def test_chunked_reverse_scan_matches_stepwise(T, B, N, K, sigma):
+    """The chunked reverse scan (tensor-core GEMM per 8-step chunk for the long-lag
+    synapses) and the step-by-step scan on the same hybrid layer: the forward is shared, so
+    the spikes are identical, and every gradient agrees within the parity tolerance."""
+    from delrec import _lib
+    case = _random_case("hybrid", 900 + N, T, B, N, sigma, False, True, True, 25.0, K)
+    outs = []
+    for variant in (_lib.REVERSE_SCAN_CHUNKED, _lib.REVERSE_SCAN_STEPWISE):
+        _lib.set_reverse_scan(variant)
+        try:
+            outs.append(run_cuda(case["meta"], case["inputs"]))
+        finally:
+            _lib.set_reverse_scan(_lib.REVERSE_SCAN_CHUNKED)
+    a, b = outs
+    assert torch.equal(a["y"], b["y"])
+    for k in ("dx", "dW", "dd", "dbias"):
+        assert rel_err(a[k], b[k]) < 1e-4, k
+    assert _lib.status() == 0
+
+
 def test_status_word_clean():
     from delrec import _lib
     assert _lib.status() == 0
 
 
 HYBRID_EDGES = [
-    # sigma, base edits, K   -> exercises offset thresholds MM = 1, 2, 3 and the per-synapse path
+    # sigma, base edits, K   -> exercises offset threshold MM = 1 and the per-synapse path
     (0.0, "zeros", 4),        # bases clamped at exactly 0: lag-0 tap has h = 0 but dh/dd != 0
     (0.5, "zeros", 4),
     (1.0, "negative", 6),     # 'centered' bases below zero
     (2.5, "negative", 8),     # window reaches > 3 lags below 1: per-synapse fallback
+    (1.5, "none", 6),         # bases U[0,6] with a wide window: two lags below 1 (MM = 2)
+    (0.0, "shift2.5", 6),     # sigma 0, bases down to -2.5 (MM = 2 or 3)
 ]
 
 
@@ -124,8 +151,10 @@ def test_hybrid_base_edges(edge):
     base = case["inputs"]["d"]
     if mode == "zeros":
         base[::3] = 0.0
-    else:
+    elif mode == "negative":
         base[::2] -= K / 2.0
+    elif mode == "shift2.5":
+        base[::2] -= 2.5
     check_case(case, name=f"hybrid_edge_sigma{sigma}_{mode}_K{K}")
 
 
