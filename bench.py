@@ -9,9 +9,10 @@ Synthetic data stands in for the SSC-shaped dataset (not available offline).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Prints one JSON line (rank 0).  ``--impl reference`` times the reference algorithm's CPU
-path (the pure-PyTorch v2 scan restated in ``oracle/``, autograd BPTT) on this host's
-cores on a bounded sample of the same workload.
+Prints one JSON line (rank 0).  ``--impl reference`` times the reference's CPU path on
+this host's cores on a bounded sample of the same workload: its own pure-PyTorch v2 scans
+(delay_layers_pytorch.py) loaded unmodified from the baseline/_ref install, or, when that
+install is absent, their restatement in ``oracle/``; autograd BPTT either way.
 """
 
 from __future__ import annotations
@@ -216,9 +217,25 @@ def max_over_ranks(v, ws):
 # ----------------------------------------------------------------------------------
 # CPU side (reference algorithm restated in oracle/)
 # ----------------------------------------------------------------------------------
-def cpu_step_fn(model, spec, cfg):
-    """A callable running one fwd+bwd of the oracle model on CPU for a batch x (T,b,C)."""
+REF_ROOT = os.path.join(ROOT, "baseline", "_ref")
+
+
+def reference_scans():
+    """The reference's own pure-PyTorch scans (delay_layers_pytorch.py, loaded unmodified
+    from the baseline/_ref install) or None when that install is absent."""
+    from oracle import reference_v2
+    try:
+        return reference_v2.load(REF_ROOT)
+    except Exception:
+        return None
+
+
+def cpu_step_fn(model, spec, cfg, ref_mod=None):
+    """A callable running one fwd+bwd of the model on CPU for a batch x (T,b,C).  The
+    recurrent delay layers run the reference's own multi_step_forward_v2 when ``ref_mod``
+    (reference_scans()) is given, else the oracle's restatement of it."""
     from oracle import delrec_oracle as O
+    from oracle import reference_v2
     from delrec import networks
     params = []
     layers = []
@@ -261,7 +278,10 @@ def cpu_step_fn(model, spec, cfg):
                 _, W, base, off, axonal = L
                 lif = O.OracleLIF(tau=cfg.tau, v_threshold=cfg.v_threshold, v_reset=cfg.v_reset,
                                   surrogate=O.ATanSpike(2.0))
-                if off is not None:
+                if ref_mod is not None:
+                    d = O.hybrid_delays(base, off) if off is not None else base
+                    h = reference_v2.scan(ref_mod, "axonal" if axonal else "synaptic", h, W, d, lif)
+                elif off is not None:
                     h = O.synaptic_scan(h, W, O.hybrid_delays(base, off), lif, sigma=0.0)
                 elif axonal:
                     h = O.axonal_scan(h, W, base, lif, sigma=0.0)
@@ -294,12 +314,13 @@ def _cpu_timed_steps(step, x, labels, warmup, steps, budget_s):
     return statistics.median(times), len(times)
 
 
-def time_cpu(model, spec, cfg, sample_b, steps, threads, warmup=1, budget_s=40.0):
+def time_cpu(model, spec, cfg, sample_b, steps, threads, warmup=1, budget_s=60.0):
     torch.set_num_threads(threads)
-    step = cpu_step_fn(model, spec, cfg)
+    ref_mod = reference_scans()
+    step = cpu_step_fn(model, spec, cfg, ref_mod)
     x, labels = make_inputs(spec, sample_b, seed=2)
     med, done = _cpu_timed_steps(step, x, labels, warmup, steps, budget_s)
-    return sample_b * spec["T"] / med, med, done
+    return sample_b * spec["T"] / med, med, done, ("reference" if ref_mod is not None else "port")
 
 
 def run_reference_arm(args, spec):
@@ -310,18 +331,23 @@ def run_reference_arm(args, spec):
     torch.set_num_threads(threads)
     model, cfg = build_model(spec, args.cpu_sample_b, "cpu")
     x, labels = make_inputs(spec, args.cpu_sample_b, seed=2)
-    step = cpu_step_fn(model, spec, cfg)
+    ref_mod = reference_scans()
+    kind = "reference" if ref_mod is not None else "port"
+    step = cpu_step_fn(model, spec, cfg, ref_mod)
     med, done = _cpu_timed_steps(step, x, labels, args.warmup, args.steps, args.cpu_budget)
     value = args.cpu_sample_b * spec["T"] / med
-    sample = (f"{args.cpu_sample_b} sample(s) x T={spec['T']} of {args.config} per step, median of "
-              f"{done} step(s) ({med:.1f} s/step; the full per-GPU batch is {spec['B']})")
+    what = ("the reference's own multi_step_forward_v2 (delay_layers_pytorch.py, from the baseline/_ref "
+            "install) with autograd BPTT" if ref_mod is not None else
+            "the oracle's restatement of the reference's v2 scan with autograd BPTT")
+    sample = (f"{args.cpu_sample_b} sample(s) x T={spec['T']} of {args.config} per step through {what}, "
+              f"median of {done} step(s) ({med:.1f} s/step; the full per-GPU batch is {spec['B']})")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "steps_timed": done, "warmup": args.warmup, "ms_per_step": med * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
             "config": {"workload": args.config, "model": spec["model"], "hidden": spec["hidden"],
                        "T": spec["T"], "batch_per_step": args.cpu_sample_b},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
                              "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -344,11 +370,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="cfg4_ssc_hybrid_2x512", choices=list(CONFIGS))
     ap.add_argument("--cpu-sample-b", type=int, default=64)
-    ap.add_argument("--cpu-steps", type=int, default=1)
+    ap.add_argument("--cpu-steps", type=int, default=3)
     ap.add_argument("--cpu-budget", type=float, default=150.0,
                     help="seconds of timed CPU steps after which the reference arm stops early")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-strong", action="store_true", help="skip the fixed-global-batch record (N > 1)")
     ap.add_argument("--T", type=int, default=None, help="override T (profiling of small cases)")
     ap.add_argument("--B", type=int, default=None, help="override the per-GPU batch")
     ap.add_argument("--hidden", type=int, default=None,
@@ -462,20 +489,62 @@ def main():
     #      steps, each bracketed by CUDA events on its own stream inside the library
     #      (every rank runs the steps: they contain the gradient all-reduce)
     roof = roofline_probe(model, step, x, labels, spec, B)
-    if roof is not None:
+    if roof is not None and "chunk_gemm" not in roof:
         smem = scan_smem_roofline(model, spec, B, roof["ms_per_launch"], clk.summary().get("sm_mhz"))
         if smem is not None:
             roof["smem"] = smem
     step_roof = step_roofline(spec, B, ms)
+    floor = latency_floor(model, spec, B)
+
+    # ---- strong scaling (BASELINE config 4 is quoted at a fixed global batch of 256):
+    #      the same step with 256 / N samples per GPU, in the same invocation
+    strong = None
+    if ws > 1 and spec["B"] % ws == 0 and not args.no_strong:
+        Bs = spec["B"] // ws
+        model_s, _ = build_model(spec, Bs, dev)
+        params_s = [p for p in model_s.parameters() if p.requires_grad]
+        opt_s = torch.optim.Adam(params_s, lr=1e-3)
+        xs = x[:, :Bs].contiguous()
+        ls = labels[:Bs].contiguous()
+
+        def step_s(xb, lb):
+            opt_s.zero_grad(set_to_none=True)
+            loss = loss_fn(model_s(xb), lb)
+            loss.backward()
+            allreduce_grads(params_s, ws)
+            opt_s.step()
+            model_s.clamp_delays()
+            return loss
+
+        for _ in range(3):
+            step_s(xs, ls)
+        ks = max(3, min(args.steps, 10))
+        barrier(ws)
+        torch.cuda.synchronize()
+        a3, b3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a3.record()
+        for _ in range(ks):
+            step_s(xs, ls)
+        b3.record()
+        torch.cuda.synchronize()
+        barrier(ws)
+        ms_s = max_over_ranks(a3.elapsed_time(b3), ws) / ks
+        strong = {"global_batch": spec["B"], "batch_per_gpu": Bs, "steps": ks, "ms_per_step": ms_s,
+                  "value": spec["B"] * spec["T"] / (ms_s / 1e3), "unit": UNIT, "scaling": "strong"}
+    elif ws == 1:
+        strong = {"global_batch": B, "batch_per_gpu": B, "steps": args.steps, "ms_per_step": ms,
+                  "value": value, "unit": UNIT, "scaling": "strong",
+                  "note": "one GPU: the main measurement (global batch = per-GPU batch)"}
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
         threads = os.cpu_count() or 1
         model_cpu, cfg_cpu = build_model(spec, args.cpu_sample_b, "cpu")
-        v, med, done = time_cpu(model_cpu, spec, cfg_cpu, args.cpu_sample_b, args.cpu_steps, threads)
-        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+        v, med, done, kind = time_cpu(model_cpu, spec, cfg_cpu, args.cpu_sample_b, args.cpu_steps, threads)
+        what = "the reference's own v2 scan" if kind == "reference" else "the oracle's v2 restatement"
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": kind,
                "sample": f"{args.cpu_sample_b} sample(s) x T={spec['T']} of the same model per step "
-                         f"(oracle fwd + autograd BPTT), median of {done} ({med:.1f} s/step)"}
+                         f"({what} fwd + autograd BPTT), median of {done} ({med:.1f} s/step)"}
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
@@ -487,7 +556,8 @@ def main():
                            "l2": "inputs larger than L2 (x is T*B*C*4 bytes per step)",
                            "firing_rates": rates},
                 "gpu_launches": launches, "clocks": clk.summary(), "e2e": e2e,
-                "roofline": roof, "step_roofline": step_roof, "cpu_baseline": cpu}
+                "roofline": roof, "step_roofline": step_roof, "latency_floor": floor,
+                "strong_scaling": strong, "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)
     if ws > 1:
         import torch.distributed as dist
@@ -532,7 +602,9 @@ def roofline_probe(model, step, x, labels, spec, B):
         for _ in range(2):
             step(x, labels)
         torch.cuda.synchronize()
-        total_ms, n = _lib.scan_time()
+        total_ms, n = _lib.scan_time(0)
+        steps_ms, n_steps = _lib.scan_time(1)
+        gemm_ms, n_gemm = _lib.scan_time(2)
     finally:
         _lib.scan_timing(False)
     if n == 0:
@@ -542,19 +614,42 @@ def roofline_probe(model, step, x, labels, spec, B):
     ms = total_ms / n
     flops = 2.0 * N * N * B * T
     peaks, src = _peaks()
-    peak = peaks["bf16_tflops_sustained"]
+    # fp32-accurate tensor rate: a 3-product bf16 split carries an fp32 contraction
+    peak = peaks["bf16_tflops_sustained"] / 3.0
     achieved = flops / (ms / 1e3) / 1e12
-    per_unit = _profiled_traffic("k_bwd_hybrid64") if spec["model"].endswith("hybrid_delays") else None
-    kern = {"hybrid": "k_bwd_hybrid64", "synaptic": "k_bwd_hybrid64 (synaptic buckets)",
-            "axonal": "k_bwd_axonal_mma or k_bwd (by size)"}
+    chunked = n_gemm > 0
+    per_unit = _profiled_traffic("k_bwd_chunk" if chunked else "k_bwd_hybrid64") \
+        if spec["model"].endswith("hybrid_delays") else None
+    kern = {"hybrid": "k_bwd_chunk steps + k_chunk_gz tensor-core chunk GEMMs" if chunked else "k_bwd_hybrid64",
+            "synaptic": "k_bwd_hybrid64 (synaptic buckets)", "axonal": "k_bwd_axonal_mma or k_bwd (by size)"}
     kind = "hybrid" if "hybrid" in spec["model"] else ("synaptic" if "synaptic" in spec["model"] else "axonal")
-    return {"bound": "tensor", "kernel": f"{kern[kind]}: reverse scan of one recurrent layer",
-            "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-            "traffic": per_unit * B * T if per_unit else None,
-            "ms_per_launch": ms, "launches_timed": n, "flops_per_launch": flops,
-            "peak_source": f"bf16_tflops_sustained ({src})",
-            "traffic_source": "ncu dram bytes per sample-timestep of a T=50 capture, scaled to B*T"
-                              if per_unit else None}
+    out = {"bound": "tensor", "kernel": f"{kern[kind]}: reverse scan of one recurrent layer",
+           "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+           "traffic": per_unit * B * T if per_unit else None,
+           "ms_per_launch": ms, "launches_timed": n, "flops_per_launch": flops,
+           "flops_definition": "2*N^2*B*T: the recurrent contraction gz = W^T gr, each synapse once",
+           "peak_source": f"bf16_tflops_sustained / 3 ({src}; fp32-accurate 3-product bf16 rate)",
+           "traffic_source": "ncu dram bytes per sample-timestep of a small-T capture, scaled to B*T"
+                             if per_unit else None}
+    if chunked:
+        # the chunk GEMMs: executed tensor-core work (every tile's 128x256 MMAs, three bf16
+        # products over the N-target reduction) against the measured sustained bf16 rate
+        K = spec["offsets"] + 1
+        ntg = (256 // K) & ~3
+        tiles = math.ceil(B / 16) * math.ceil(N / ntg)
+        nchunks = math.ceil(T / 8)
+        exec_flops = tiles * 2.0 * 128 * 256 * (math.ceil(N / 64) * 64) * 3 * nchunks
+        layers = n
+        g_ms = gemm_ms / layers
+        out["chunk_gemm"] = {"kernel": "k_chunk_gz", "ms_per_layer": g_ms, "launches_per_layer": n_gemm / layers,
+                             "executed_tflops": exec_flops / (g_ms / 1e3) / 1e12,
+                             "peak_tflops": peaks["bf16_tflops_sustained"],
+                             "frac": exec_flops / (g_ms / 1e3) / 1e12 / peaks["bf16_tflops_sustained"],
+                             "executed_flops_per_layer": exec_flops}
+        out["chunk_steps"] = {"kernel": "k_bwd_chunk", "ms_per_layer": steps_ms / layers,
+                              "launches_per_layer": n_steps / layers,
+                              "us_per_timestep": steps_ms / layers * 1e3 / T}
+    return out
 
 
 SMEM_BYTES_PER_CLK_SM = 128   # shared-memory bandwidth per SM (32 banks x 4 bytes)
@@ -580,6 +675,26 @@ def scan_smem_roofline(model, spec, B, ms, sm_mhz):
     return {"bound": "smem", "achieved": achieved, "peak": peak, "unit": "TB/s", "frac": achieved / peak,
             "bytes_per_launch": nbytes,
             "peak_source": f"128 B/clk/SM x {N_SMS} SMs at the sampled median {sm_mhz:.0f} MHz"}
+
+
+def latency_floor(model, spec, B):
+    """The reverse scans' per-step exchange alone (delrec_exchange_floor: publish gr to L2,
+    meet the batch tile, restage gr into shared memory; no LIF, no synapse sums) over T
+    steps on the tiling the layer's scan uses, times the number of recurrent layers: the
+    latency floor of the step-by-step part of the backward."""
+    from delrec import _lib
+    rec = [m for m in model.layers if hasattr(m, "recurrent_weights")]
+    if not rec:
+        return None
+    N, T = rec[0].neurons, spec["T"]
+    try:
+        f_ms = _lib.exchange_floor_ms(T, B, N)
+    except RuntimeError:
+        return None
+    return {"ms_per_layer": f_ms, "layers": len(rec), "ms_per_step": f_ms * len(rec),
+            "us_per_timestep": f_ms * 1e3 / T,
+            "what": "T steps of the per-step gr exchange (L2 publish, tile arrival counter, "
+                    "shared-memory restage) on the scan's grid, no compute"}
 
 
 def step_algorithmic(spec, B):
@@ -619,10 +734,15 @@ def step_roofline(spec, B, ms):
     t_flops = flops / (p_fp32acc * 1e12)
     t_bytes = nbytes / (peaks["hbm_gbs"] * 1e9)
     floor_ms = max(t_flops, t_bytes) * 1e3
+    # the same floor with the fp32 CUDA-core rate (148 SMs x 128 FMA/clk x 2 at the max
+    # SM clock): the fraction a SIMT-only implementation could reach
+    p_simt = 148 * 128 * 2 * peaks.get("sm_max_mhz", 1965.0) * 1e6 / 1e12
+    simt_ms = max(flops / (p_simt * 1e12), t_bytes) * 1e3
     return {"flops": flops, "bytes": nbytes, "floor_ms": floor_ms,
             "bound": "tensor" if t_flops >= t_bytes else "hbm", "frac": floor_ms / ms,
             "peak_tflops_fp32acc": p_fp32acc, "peak_hbm_gbs": peaks["hbm_gbs"],
-            "peak_source": f"bf16_tflops_sustained/3 and hbm_gbs ({src})"}
+            "peak_source": f"bf16_tflops_sustained/3 and hbm_gbs ({src})",
+            "simt_floor_ms": simt_ms, "simt_frac": simt_ms / ms, "peak_tflops_fp32_simt": p_simt}
 
 
 if __name__ == "__main__":

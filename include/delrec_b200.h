@@ -253,6 +253,9 @@ unsigned long long delrec_launch_count(void);
  * returns the summed milliseconds and the number of launches since enabling. */
 int delrec_scan_timing(int enable);
 int delrec_scan_time(double* total_ms, int* launches);
+/* The same per part: 0 = every reverse scan (a chunked scan counts as one launch per
+ * layer), 1 = the step launches of the chunked scans, 2 = their chunk GEMM launches. */
+int delrec_scan_time_part(int part, double* total_ms, int* launches);
 /* Reverse-scan variant of the layer backwards (process-wide).  0 (default): hybrid layers
  * whose shape allows it run the chunked scan -- the delayed-gradient contraction of every
  * synapse whose lag reaches past the current 8-step chunk as one tensor-core GEMM per
@@ -261,6 +264,14 @@ int delrec_scan_time(double* total_ms, int* launches);
  * cover either variant.  Replaces no reference call (the reference has one Triton
  * kernel per layer kind, triton_kernels/synaptic_eventdriven.py:323-364). */
 int delrec_set_reverse_scan(int variant);
+/* Measurement: the per-step latency floor of the reverse scans.  Runs T steps of their
+ * exchange alone -- each block publishes its slice of gr to L2, meets its batch tile at an
+ * arrival counter and restages the tile's gr into shared memory -- on the grid and tiling
+ * the 64-sample scans use for `layer` (N <= 512, B > 32; otherwise
+ * DELREC_ERR_UNSUPPORTED), with no LIF step and no synapse sums.  Time it with events on
+ * `stream`.  No counterpart in the reference. */
+size_t delrec_exchange_floor_workspace(const delrec_layer* layer);
+int delrec_exchange_floor(const delrec_layer* layer, void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

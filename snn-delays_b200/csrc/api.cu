@@ -50,14 +50,17 @@ static unsigned long long g_launches = 0;  // kernels issued by this library (ho
 // Optional timing of the reverse-scan kernels: CUDA events recorded on the launching
 // stream around each scan launch while enabled (delrec_scan_timing).
 static bool g_scan_timing = false;
-static cudaEvent_t g_ev[512][2];
-static int g_ev_n = 0;
-static void scan_mark(int which, cudaStream_t st) {
-  if (!g_scan_timing || g_ev_n >= 512) return;
-  cudaEvent_t& e = g_ev[g_ev_n][which];
+// part 0: whole reverse-scan launches (or the whole chunked scan of a layer); 1: the step
+// launches of the chunked scan; 2: its chunk GEMM launches
+static constexpr int kTimeParts = 3, kTimeSlots = 1024;
+static cudaEvent_t g_ev[kTimeParts][kTimeSlots][2];
+static int g_ev_n[kTimeParts] = {0, 0, 0};
+static void scan_mark(int which, cudaStream_t st, int part = 0) {
+  if (!g_scan_timing || part < 0 || part >= kTimeParts || g_ev_n[part] >= kTimeSlots) return;
+  cudaEvent_t& e = g_ev[part][g_ev_n[part]][which];
   if (!e) cudaEventCreate(&e);
   cudaEventRecord(e, st);
-  if (which == 1) ++g_ev_n;
+  if (which == 1) ++g_ev_n[part];
 }
 
 #define DR_LAUNCHED()                                                      \
@@ -979,10 +982,10 @@ static ChunkPlan plan_chunk(const delrec_layer* ly, const BwdPlan& bp, const Hyb
   if (!h64.ok || ly->kind != DELREC_HYBRID) return c;
   c.KP1 = h64.K + 1;
   if (c.KP1 > kChunk + 1 || bp.TAPS > kH64Taps) return c;
-  c.ntiles = cdiv(ly->N, kGzCols / c.KP1);
+  c.ntiles = cdiv(ly->N, gz_ntg(c.KP1));
   c.nchunks = cdiv(ly->T, kChunk);
   c.Np = pad8(ly->N);
-  c.smem = hyb64_smem_plan(ly->N, h64.NT, h64.CAPS, h64.K, bp.TAPS, kChunk).total;
+  c.smem = hyb64_smem_plan(ly->N, h64.NT, h64.CAPS, h64.K, bp.TAPS, kChunk).total + align256((size_t)ly->N * 4);
   c.ok = c.smem <= kSmemLimit;
   return c;
 }
@@ -1070,18 +1073,23 @@ static int run_chunked(const delrec_layer* ly, const Hyb64Plan& h64, const Chunk
   a.lif = base.lif; a.grx = base.grx; a.arrive = base.arrive; a.spin_limit = base.spin_limit;
   GzArgs g{};
   g.T = T; g.B = B; g.N = N; g.gz = gz; g.spin_ns = 2000000000ll;
+  DR_CUDA(cudaMemsetAsync(a.arrive, 0, sizeof(unsigned int) * h64.tiles, st));
   scan_mark(0, st);
   for (int ch = cp.nchunks - 1; ch >= 0; --ch) {
     a.t0 = ch * kChunk;
     a.t_hi = std::min(T - 1, a.t0 + kChunk - 1);
-    DR_CUDA(cudaMemsetAsync(a.arrive, 0, sizeof(unsigned int) * h64.tiles, st));
+    a.arr_base = (unsigned int)((T - 1 - a.t_hi) * h64.CS);
     ChunkArgs ac = a;
     void* args[] = {(void*)&ac};
+    scan_mark(0, st, 1);
     DR_CUDA(cudaLaunchCooperativeKernel((const void*)kern, dim3(h64.CS * h64.tiles), dim3(kH64Threads), args,
                                         cp.smem, st));
+    scan_mark(1, st, 1);
     ++g_launches;
     g.t0 = a.t0;
+    scan_mark(0, st, 2);
     rc = launch_gz(cp.KP1, maps, g, cp.ntiles, st);
+    scan_mark(1, st, 2);
     if (rc) return rc;
   }
   scan_mark(1, st);
@@ -1396,22 +1404,66 @@ unsigned long long delrec_launch_count(void) { return g_launches; }
 
 int delrec_scan_timing(int enable) {
   g_scan_timing = enable != 0;
-  g_ev_n = 0;
+  for (int p = 0; p < kTimeParts; ++p) g_ev_n[p] = 0;
   return DELREC_OK;
 }
-
-int delrec_scan_time(double* total_ms, int* launches) {
-  if (!total_ms || !launches) return DELREC_ERR_ARG;
+int delrec_scan_time_part(int part, double* total_ms, int* launches) {
+  if (!total_ms || !launches || part < 0 || part >= kTimeParts) return DELREC_ERR_ARG;
   double sum = 0.0;
-  for (int i = 0; i < g_ev_n; ++i) {
-    DR_CUDA(cudaEventSynchronize(g_ev[i][1]));
+  for (int i = 0; i < g_ev_n[part]; ++i) {
+    DR_CUDA(cudaEventSynchronize(g_ev[part][i][1]));
     float ms = 0.f;
-    DR_CUDA(cudaEventElapsedTime(&ms, g_ev[i][0], g_ev[i][1]));
+    DR_CUDA(cudaEventElapsedTime(&ms, g_ev[part][i][0], g_ev[part][i][1]));
     sum += ms;
   }
   *total_ms = sum;
-  *launches = g_ev_n;
-  g_ev_n = 0;
+  *launches = g_ev_n[part];
+  g_ev_n[part] = 0;
+  return DELREC_OK;
+}
+int delrec_scan_time(double* total_ms, int* launches) { return delrec_scan_time_part(0, total_ms, launches); }
+
+// The reverse scans' exchange alone (k_exchange_floor) on the tiling the 64-sample scans
+// use for this layer: a measurement of the per-step latency floor.
+static int floor_plan(const delrec_layer* ly, Hyb64Plan* h) {
+  if (!ly || ly->T < 1 || ly->B < 1 || ly->N < 1) return DELREC_ERR_ARG;
+  delrec_layer l = *ly;
+  l.kind = DELREC_HYBRID;
+  if (l.K < 0) l.K = 0;
+  const BwdPlan bp = plan_backward(&l, DELREC_HYBRID);
+  *h = plan_hybrid64(&l, bp);
+  return h->ok ? DELREC_OK : DELREC_ERR_UNSUPPORTED;
+}
+size_t delrec_exchange_floor_workspace(const delrec_layer* ly) {
+  Hyb64Plan h{};
+  if (floor_plan(ly, &h)) return 0;
+  Carve c(nullptr, (size_t)-1);
+  c.take<float>((size_t)2 * h.tiles * ly->N * kH64BT);
+  c.take<unsigned int>((size_t)h.tiles);
+  return c.off;
+}
+int delrec_exchange_floor(const delrec_layer* ly, void* ws, size_t wsb, void* stream) {
+  Hyb64Plan h{};
+  int rc = floor_plan(ly, &h);
+  if (rc) return rc;
+  if (((uintptr_t)ws & 255) != 0 || wsb < delrec_exchange_floor_workspace(ly)) return DELREC_ERR_WORKSPACE;
+  cudaStream_t st = (cudaStream_t)stream;
+  Carve c(ws, wsb);
+  float* grx = c.take<float>((size_t)2 * h.tiles * ly->N * kH64BT);
+  unsigned int* arrive = c.take<unsigned int>((size_t)h.tiles);
+  if (!c.ok) return DELREC_ERR_WORKSPACE;
+  rc = set_smem(k_exchange_floor, h.smem);
+  if (rc) return rc;
+  int per_sm = 0;
+  DR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_exchange_floor, kH64Threads, h.smem));
+  if (per_sm < 1 || h.CS * h.tiles > per_sm * kSMs) return DELREC_ERR_UNSUPPORTED;
+  DR_CUDA(cudaMemsetAsync(arrive, 0, sizeof(unsigned int) * h.tiles, st));
+  int T = ly->T, N = ly->N, CS = h.CS, NT = h.NT;
+  long long spin = 1ll << 22;
+  void* args[] = {(void*)&T, (void*)&N, (void*)&CS, (void*)&NT, (void*)&grx, (void*)&arrive, (void*)&spin};
+  DR_CUDA(cudaLaunchCooperativeKernel((const void*)k_exchange_floor, dim3(h.CS * h.tiles), dim3(kH64Threads), args,
+                                      h.smem, st));
+  ++g_launches;
   return DELREC_OK;
 }
 

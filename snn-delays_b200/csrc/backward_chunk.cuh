@@ -57,7 +57,8 @@ struct ChunkArgs {
   float* lam;              // (B, N) LIF gradient carried from step t0 to step t0 - 1
   LifK lif;
   float* grx;              // [2][tiles][N][64] exchange of gr(t)
-  unsigned int* arrive;    // [tiles] arrival counters, zero at launch
+  unsigned int* arrive;    // [tiles] arrival counters, zeroed once before the first chunk
+  unsigned int arr_base;   // arrivals per tile published by the earlier chunks of this scan
   long long spin_limit;
 };
 
@@ -89,6 +90,7 @@ __global__ void __launch_bounds__(512, 1) k_bwd_chunk(ChunkArgs a) {
   int* tnt = tl0 + NT;
   float* tw = (float*)(tnt + NT);                                              // [NT][TAPS]
   float* ring = (float*)(smem + P.grc + P.idx + P.w + P.boff + P.taps);        // [NT][RS]
+  int* rowq = (int*)(smem + P.total);                                          // [N]
 
   // ---- init: the short buckets (k <= C - 1 - l0) of the block's sources, taps, ring
   for (int e = tid; e < NT * a.CAPS; e += NTH) {
@@ -123,7 +125,21 @@ __global__ void __launch_bounds__(512, 1) k_bwd_chunk(ChunkArgs a) {
     tw[e] = ol < nts ? a.tap_w[(size_t)(o0 + ol) * a.TAPS + (e % a.TAPS)] : 0.f;
   }
   for (int e = tid; e < NT * RS; e += NTH) ring[e] = 0.f;
+  for (int i = tid; i < N; i += NTH) rowq[i] = RING;
   if (tid == 0) s_abort = 0;
+  __syncthreads();
+  // rowq[i]: the first chunk position q (gr(t0 + q) staged at step t0 + q) from which a
+  // short synapse of this block reads target row i: l0_o + k over the entries of bucket k
+  for (int e = tid; e < NT * a.CAPS; e += NTH) {
+    const int ol = e / a.CAPS, pos = e % a.CAPS;
+    if (ol >= nts) continue;
+    const int l0 = tl0[ol];
+    const int kl = min(K, RING - 1 - l0);
+    if (kl < 0 || pos >= sbo[ol * (K + 2) + kl + 1]) continue;
+    int k = 0;
+    while (k < kl && pos >= sbo[ol * (K + 2) + k + 1]) ++k;
+    atomicMin(&rowq[sidx[e]], l0 + k);
+  }
   __syncthreads();
 
   int pol[PPT], pbl[PPT];
@@ -186,7 +202,7 @@ __global__ void __launch_bounds__(512, 1) k_bwd_chunk(ChunkArgs a) {
   const bool w_ok = ol_w < nts;
   const bool w_urg = w_ok && surg[ol_w];
   const int w_l0 = w_ok ? tl0[ol_w] : RING;
-  unsigned int arrivals = 0;
+  unsigned int arrivals = a.arr_base;
   const size_t xtile = (size_t)N * BT;
 
   for (int t = t_hi; t >= t0; --t) {
@@ -277,10 +293,13 @@ __global__ void __launch_bounds__(512, 1) k_bwd_chunk(ChunkArgs a) {
       __syncthreads();
       if (s_abort) return;
       {
+        // only the rows a short synapse of this block reads from gr(t) (position t - t0)
+        const int q = t - t0;
         const int n4 = N * BT / 4;
         const float4* xs = (const float4*)xb;
         float4* gd = (float4*)grc;
-        for (int v = tid; v < n4; v += NTH) gd[v] = __ldcg(xs + v);
+        for (int v = tid; v < n4; v += NTH)
+          if (rowq[v >> 4] <= q) gd[v] = __ldcg(xs + v);
       }
       __syncthreads();
       // ===== C2: offset 0 of a source with a lag-1 tap (read at step t - 1)
@@ -305,8 +324,56 @@ __global__ void __launch_bounds__(512, 1) k_bwd_chunk(ChunkArgs a) {
     if (pok[k]) a.lam[(size_t)(b0 + pbl[k]) * N + o0 + pol[k]] = lam[k];
 }
 
+// The latency floor of the step-by-step part of the reverse scans: the same grid, block
+// size, shared memory and per-tile exchange as k_bwd_chunk / k_bwd_hybrid64, but nothing
+// else -- per step each block publishes its slice of the tile's gr row block to L2,
+// release-arrives at the tile counter, waits for the tile and restages the tile's N x 64
+// values into shared memory.  T steps of it bound any scan that exchanges gr every step.
+__global__ void __launch_bounds__(512, 1) k_exchange_floor(int T, int N, int CS, int NT, float* grx,
+                                                           unsigned int* arrive, long long spin_limit) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ int s_abort;
+  float* grc = (float*)smem;   // [N][64]
+  constexpr int BT = kH64BT, NTH = kH64Threads;
+  const int tid = threadIdx.x;
+  const int rank = (int)(blockIdx.x % CS), tile = (int)(blockIdx.x / CS), tiles = (int)(gridDim.x / CS);
+  const int o0 = rank * NT, nts = max(0, min(NT, N - o0));
+  const size_t xtile = (size_t)N * BT;
+  for (int e = tid; e < N * BT; e += NTH) grc[e] = 0.f;
+  if (tid == 0) s_abort = 0;
+  __syncthreads();
+  unsigned int arrivals = 0;
+  for (int t = T - 1; t >= 0; --t) {
+    float* xb = grx + ((size_t)(t & 1) * tiles + tile) * xtile;
+    for (int e = tid; e < nts * BT; e += NTH) __stcg(xb + (size_t)o0 * BT + e, grc[(size_t)o0 * BT + e]);
+    __syncthreads();
+    if (tid == 0) {
+      asm volatile("fence.acq_rel.gpu;" ::: "memory");
+      atomicAdd(arrive + tile, 1u);
+    }
+    arrivals += CS;
+    if (tid == 0) {
+      long long polls = 0;
+      unsigned int seen;
+      do {
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(seen) : "l"(arrive + tile) : "memory");
+        if (++polls > spin_limit) { flag_status(ST_TIMEOUT); s_abort = 1; break; }
+      } while (seen < arrivals);
+    }
+    __syncthreads();
+    if (s_abort) return;
+    const float4* xs = (const float4*)xb;
+    float4* gd = (float4*)grc;
+    for (int v = tid; v < N * BT / 4; v += NTH) gd[v] = __ldcg(xs + v);
+    __syncthreads();
+  }
+}
+
 // ---- the chunk GEMM ---------------------------------------------------------------------
 constexpr int kGzRows = 128, kGzCols = 256, kGzSamples = kGzRows / kChunk, kGzStages = 2;
+// sources per column tile: as many as 256 columns hold, rounded down to a multiple of 4 (the
+// epilogue adds groups of 4 consecutive sources with one vector reduction)
+__host__ __device__ constexpr int gz_ntg(int KP1) { return (kGzCols / KP1) & ~3; }
 constexpr uint32_t kGzABytes = kGzRows * 64 * 2, kGzBBytes = kGzCols * 64 * 2;
 constexpr uint32_t kGzStageBytes = 2 * kGzABytes + 2 * kGzBBytes;
 constexpr size_t kGzSmem = (size_t)kGzStages * kGzStageBytes + 1024;
@@ -317,6 +384,11 @@ struct GzArgs {
   long long spin_ns;
 };
 
+// gz[0..3] += v (one vector reduction; gz 16-byte aligned)
+__device__ __forceinline__ void red_add_v4(float* gz, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(gz), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
@@ -326,7 +398,7 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
 }
 
 // One CTA: 16 samples x the chunk's 8 steps (rows b*8 + q) against 256 (source, offset)
-// columns (source-major, KP1 = K+1 offsets per source, 256 / KP1 sources per tile).
+// columns (source-major, KP1 = K+1 offsets per source, gz_ntg(KP1) sources per tile).
 // A = gr pieces from the (B, T, Np) layout through a 3-D tensor map (box 64 x 8 x 16),
 // B = the offset-masked W pieces (tile rows of 256, K-major).  Two pipeline stages of all
 // four pieces of a 64-wide reduction block; per block 12 MMAs (3 products x 4 K-steps).
@@ -337,7 +409,7 @@ __global__ void __launch_bounds__(128, 1)
     k_chunk_gz(const __grid_constant__ CUtensorMap mahi, const __grid_constant__ CUtensorMap malo,
                const __grid_constant__ CUtensorMap mbhi, const __grid_constant__ CUtensorMap mblo, const GzArgs g) {
   static_assert(KP1 >= 1 && KP1 <= kChunk + 1, "offset window wider than two chunks");
-  constexpr int NTG = kGzCols / KP1, USED = NTG * KP1;
+  constexpr int NTG = gz_ntg(KP1), USED = NTG * KP1;
   extern __shared__ unsigned char dsm[];
   __shared__ __align__(8) uint64_t bars[2 * kGzStages + 1];
   __shared__ uint32_t s_tmem;
@@ -414,9 +486,17 @@ __global__ void __launch_bounds__(128, 1)
   const bool brow = ok && b < g.B;
   const size_t BN = (size_t)g.B * g.N;
   const int s0 = t0 + q, s1 = t0 + q - kChunk;
-  float acc0 = 0.f, acc1 = 0.f;
+  // gz rows of this thread's two output steps; each group of 4 consecutive sources is one
+  // vector reduction when N is a multiple of 4 (rows 16-byte aligned), else 4 scalar ones
+  float* row0 = (brow && s0 < g.T) ? g.gz + (size_t)s0 * BN + (size_t)b * g.N : nullptr;
+  float* row1 = (brow && s1 >= 0) ? g.gz + (size_t)s1 * BN + (size_t)b * g.N : nullptr;
+  const bool vec = (g.N & 3) == 0;
+  float a0[4], a1[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) a0[i] = a1[i] = 0.f;
 #pragma unroll
   for (int cc = 0; cc < kGzCols / 32; ++cc) {
+    if (cc * 32 >= USED) break;
     float v[32];
     if (ok) {
       tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(cc * 32), v);
@@ -428,19 +508,25 @@ __global__ void __launch_bounds__(128, 1)
     for (int jj = 0; jj < 32; ++jj) {
       const int c = cc * 32 + jj;
       if (c < USED) {
-        const int k = c % KP1;
+        const int k = c % KP1, ol = c / KP1, g4 = ol & 3;
         const int src = q + k;   // lane of row tau = t0 + src (window 0) or t0 + src - 8
         const float x = __shfl_sync(0xffffffffu, v[jj], grp | (src & 7));
-        if (src < kChunk) acc0 += x;
-        else acc1 += x;
-        if (k == KP1 - 1) {
-          const int o = ob + c / KP1;
-          if (brow && o < g.N) {
-            if (s0 < g.T) atomicAdd(g.gz + (size_t)s0 * BN + (size_t)b * g.N + o, acc0);
-            if (s1 >= 0) atomicAdd(g.gz + (size_t)s1 * BN + (size_t)b * g.N + o, acc1);
+        if (src < kChunk) a0[g4] += x;
+        else a1[g4] += x;
+        if (k == KP1 - 1 && g4 == 3) {   // sources ol-3 .. ol complete
+          const int o = ob + ol - 3;
+          if (vec) {
+            if (row0 && o < g.N) red_add_v4(row0 + o, a0[0], a0[1], a0[2], a0[3]);
+            if (row1 && o < g.N) red_add_v4(row1 + o, a1[0], a1[1], a1[2], a1[3]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              if (row0 && o + i < g.N) atomicAdd(row0 + o + i, a0[i]);
+              if (row1 && o + i < g.N) atomicAdd(row1 + o + i, a1[i]);
+            }
           }
-          acc0 = 0.f;
-          acc1 = 0.f;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) a0[i] = a1[i] = 0.f;
         }
       }
     }
@@ -452,13 +538,13 @@ __global__ void __launch_bounds__(128, 1)
 }
 
 // Offset-masked W as the GEMM's B operand: row r = tile * 256 + c, c = ol * KP1 + k
-// (source o = tile * (256 / KP1) + ol, offset k), column i (target):
+// (source o = tile * gz_ntg(KP1) + ol, offset k), column i (target):
 // value W[i, o] if offsets[i, o] == k, else 0; written as bf16 hi + lo pieces with row
 // stride Np (columns >= N and unused rows are zero).
 __global__ void k_mask_w(int N, int Np, int KP1, int rows, const float* __restrict__ W,
                          const uint8_t* __restrict__ offT, __nv_bfloat16* __restrict__ hi,
                          __nv_bfloat16* __restrict__ lo) {
-  const int NTG = kGzCols / KP1;
+  const int NTG = gz_ntg(KP1);
   const size_t total = (size_t)rows * Np;
   for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
     const int r = (int)(e / Np), i = (int)(e % Np);

@@ -82,7 +82,10 @@ _SIGS = {
     "delrec_launch_count": (ctypes.c_ulonglong, []),
     "delrec_scan_timing": (_I, [_I]),
     "delrec_scan_time": (_I, [_P, _P]),
+    "delrec_scan_time_part": (_I, [_I, _P, _P]),
     "delrec_set_reverse_scan": (_I, [_I]),
+    "delrec_exchange_floor_workspace": (_S, [_P]),
+    "delrec_exchange_floor": (_I, [_P, _P, _S, _P]),
 }
 
 _lib = None
@@ -168,11 +171,12 @@ def scan_timing(enable: bool):
     check(lib().delrec_scan_timing(int(enable)), "delrec_scan_timing")
 
 
-def scan_time():
-    """(total milliseconds, launches) of the reverse-scan kernels timed since enabling."""
+def scan_time(part=0):
+    """(total milliseconds, launches) of the reverse-scan kernels timed since enabling:
+    part 0 every scan, 1 the step launches of the chunked scans, 2 their chunk GEMMs."""
     ms = ctypes.c_double(0.0)
     n = ctypes.c_int(0)
-    check(lib().delrec_scan_time(ctypes.byref(ms), ctypes.byref(n)), "delrec_scan_time")
+    check(lib().delrec_scan_time_part(int(part), ctypes.byref(ms), ctypes.byref(n)), "delrec_scan_time_part")
     return ms.value, n.value
 
 
@@ -184,6 +188,28 @@ def set_reverse_scan(variant: int):
     (default: hybrid layers contract their long-lag synapses once per 8-step chunk on the
     tensor cores) or REVERSE_SCAN_STEPWISE (the step-by-step scans only)."""
     check(lib().delrec_set_reverse_scan(int(variant)), "delrec_set_reverse_scan")
+
+
+def exchange_floor_ms(T, B, N, K=0, repeats=3, device=None):
+    """Milliseconds of the reverse scans' per-step exchange alone over T steps (the latency
+    floor of one layer's scan) on the tiling used for a (T, B, N) layer; the median of
+    ``repeats`` launches timed with CUDA events on the current stream."""
+    import statistics
+    layer = Layer(HYBRID, int(T), int(B), int(N), 2, int(K), 0, 0, 1.0, 0.0)
+    nbytes = lib().delrec_exchange_floor_workspace(ctypes.byref(layer))
+    if nbytes == 0:
+        raise RuntimeError("delrec_b200: no exchange-floor tiling for this shape")
+    ws = workspace(nbytes, device or torch.cuda.current_device())
+    st = stream_ptr(device)
+    times = []
+    for _ in range(repeats + 1):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        check(lib().delrec_exchange_floor(ctypes.byref(layer), ptr(ws), nbytes, st), "delrec_exchange_floor")
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    return statistics.median(times[1:])
 
 
 def status() -> int:

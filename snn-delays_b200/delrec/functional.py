@@ -41,6 +41,41 @@ def ring_length(d_max, s_max) -> int:
     return int(torch.ceil(1.0 + d_max + s_max).item()) + 1
 
 
+# Host copies of device-side reductions that size the kernel launches (largest delay,
+# widest triangle, smallest base, largest offset).  They are read back (one host
+# synchronisation) only when a tensor they depend on changed since the last call: a
+# tensor is identified by the object itself and its in-place version counter, which an
+# optimizer step or a clamp_ advances, so a training step syncs once per layer and
+# repeated forwards between two updates (evaluation, micro-batches) do not sync at all.
+_STATS: dict = {}
+
+
+def _cached_stats(tag, tensors, compute):
+    import weakref
+    key = (tag,) + tuple(id(t) if t is not None else None for t in tensors)
+    try:
+        vers = tuple(t._version if t is not None else None for t in tensors)
+    except RuntimeError:   # inference-mode tensors carry no version counter
+        return compute()
+    hit = _STATS.get(key)
+    if hit is not None:
+        refs, v, vals = hit
+        if v == vers and all((r() is t) if t is not None else r is None for r, t in zip(refs, tensors)):
+            return vals
+    vals = compute()
+    if len(_STATS) > 512:
+        _STATS.clear()
+    _STATS[key] = (tuple(weakref.ref(t) if t is not None else None for t in tensors), vers, vals)
+    return vals
+
+
+def _s_max(sigma, p_spread, use_sig_p, s):
+    """The widest half-width: a host value unless the widths are learned per source."""
+    if use_sig_p:
+        return None
+    return 1.0 + float(sigma)
+
+
 def surrogate_params(config):
     """(surrogate id, gamma, alpha) exactly as the reference's shims derive them from
     ``config.surrogate_function`` (delay_layers_triton.py:28-35, 58)."""
@@ -182,11 +217,17 @@ class AxonalRecdelTriton(torch.autograd.Function):
                                       "not provided; use round_delays for an STE-rounded forward")
         T, B, N = x.shape
         s = half_widths(sigma, p_spread, use_sig_p, N, x.device)
-        L = ring_length(d.detach().max(), s.max())
+        sm = _s_max(sigma, p_spread, use_sig_p, s)
+        if sm is None:
+            dmax, sm = _cached_stats(("ax", float(sigma)), (d, p_spread),
+                                     lambda: torch.stack([d.detach().max().float(), s.max()]).tolist())
+        else:
+            dmax = _cached_stats("ax", (d,), lambda: [float(d.detach().max())])[0]
+        L = ring_length(torch.tensor(dmax, dtype=torch.float32), torch.tensor(sm, dtype=torch.float32))
         lif = _lib.lif_struct(tau, v_th, v_reset, detach_reset, surr_id, gamma, alpha)
         keep = _keep2d(drop, B, N)
         b = bias.detach().float().contiguous() if bias is not None else None
-        y, u, desc = layer_forward(_lib.AXONAL, x, W, b, d, None, s, keep, L, 0, lif)
+        y, u, desc = layer_forward(_lib.AXONAL, x, W, b, d, None, s, keep, L, 0, lif, s_max=sm)
         ctx.save_for_backward(u, y, W, d, s, keep if keep is not None else torch.empty(0), p_spread)
         ctx.meta = (desc, lif, sigma, use_sig_p, keep is not None)
         return y
@@ -222,11 +263,18 @@ class EventDrivenSyn(torch.autograd.Function):
         T, B, N = x.shape
         d_eff = _effective_d(d, layer).float().contiguous()
         s = half_widths(layer.sigma, p_spread, layer.use_sig_p, N, x.device)
-        L = ring_length(d_eff.max(), s.max())
+        rnd = bool(getattr(layer, "round_delays", False))
+        sm = _s_max(layer.sigma, p_spread, layer.use_sig_p, s)
+        if sm is None:
+            dmax, sm = _cached_stats(("syn", rnd, float(layer.sigma)), (d, p_spread),
+                                     lambda: torch.stack([d_eff.max(), s.max()]).tolist())
+        else:
+            dmax = _cached_stats(("syn", rnd), (d,), lambda: [float(d_eff.max())])[0]
+        L = ring_length(torch.tensor(dmax, dtype=torch.float32), torch.tensor(sm, dtype=torch.float32))
         lif = lif_from_layer(layer)
         keep = _keep2d(drop, B, N)
         b = bias.detach().float().contiguous() if bias is not None else None
-        y, u, desc = layer_forward(_lib.SYNAPTIC, x, W, b, d_eff, None, s, keep, L, 0, lif)
+        y, u, desc = layer_forward(_lib.SYNAPTIC, x, W, b, d_eff, None, s, keep, L, 0, lif, s_max=sm)
         ctx.save_for_backward(u, y, W, d_eff, s, keep if keep is not None else torch.empty(0), p_spread)
         ctx.meta = (desc, lif, float(layer.sigma), bool(layer.use_sig_p), keep is not None)
         return y
@@ -295,8 +343,12 @@ class HybridBaseDelay(torch.autograd.Function):
         base_eff = _effective_d(base, layer).float().contiguous()
         off = offsets.detach().float().contiguous()
         s = half_widths(layer.sigma, p_spread, layer.use_sig_p, N, x.device)
-        # one host sync for every scalar the launch needs
-        stats = torch.stack([base_eff.max() + off.max(), s.max(), base_eff.min(), off.max()]).tolist()
+        # every scalar the launch needs, read back once per update of base / p_spread
+        rnd = bool(getattr(layer, "round_delays", False))
+        stats = _cached_stats(("hyb", rnd, float(layer.sigma), bool(layer.use_sig_p)),
+                              (base, offsets, p_spread if layer.use_sig_p else None),
+                              lambda: torch.stack([base_eff.max() + off.max(), s.max(), base_eff.min(),
+                                                   off.max()]).tolist())
         dmax, s_max, base_min, off_max = stats
         K = int(round(off_max)) if off.numel() else 0
         L = int(math.ceil(1.0 + dmax + s_max)) + 1
