@@ -985,7 +985,7 @@ static ChunkPlan plan_chunk(const delrec_layer* ly, const BwdPlan& bp, const Hyb
   c.ntiles = cdiv(ly->N, gz_ntg(c.KP1));
   c.nchunks = cdiv(ly->T, kChunk);
   c.Np = pad8(ly->N);
-  c.smem = hyb64_smem_plan(ly->N, h64.NT, h64.CAPS, h64.K, bp.TAPS, kChunk).total + align256((size_t)ly->N * 4);
+  c.smem = hyb64_smem_plan(ly->N, h64.NT, h64.CAPS, h64.K, bp.TAPS, kChunk).total;
   c.ok = c.smem <= kSmemLimit;
   return c;
 }
@@ -1018,7 +1018,10 @@ static int launch_gz_t(const CUtensorMap* m, const GzArgs& g, int ntiles, cudaSt
   auto kern = k_chunk_gz<KP1>;
   int rc = set_smem(kern, kGzSmem);
   if (rc) return rc;
-  kern<<<dim3(cdiv(g.B, kGzSamples), ntiles), 128, kGzSmem, st>>>(m[0], m[1], m[2], m[3], g);
+  GzArgs ga = g;
+  ga.ntiles = ntiles;
+  const int total = cdiv(g.B, kGzSamples) * ntiles;
+  kern<<<std::min(total, kSMs), kGzThreads, kGzSmem, st>>>(m[0], m[1], m[2], m[3], ga);
   DR_LAUNCHED();
   return DELREC_OK;
 }

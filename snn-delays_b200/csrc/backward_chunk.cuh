@@ -90,20 +90,14 @@ __global__ void __launch_bounds__(512, 1) k_bwd_chunk(ChunkArgs a) {
   int* tnt = tl0 + NT;
   float* tw = (float*)(tnt + NT);                                              // [NT][TAPS]
   float* ring = (float*)(smem + P.grc + P.idx + P.w + P.boff + P.taps);        // [NT][RS]
-  int* rowq = (int*)(smem + P.total);                                          // [N]
 
-  // ---- init: the short buckets (k <= C - 1 - l0) of the block's sources, taps, ring
-  for (int e = tid; e < NT * a.CAPS; e += NTH) {
-    const int ol = e / a.CAPS, pos = e % a.CAPS;
-    int2 en = make_int2(0, 0);
-    if (ol < nts) {
-      const int o = o0 + ol;
-      const int kl = min(K, RING - 1 - a.tap_l0[o]);
-      const int tot = kl >= 0 ? a.boff[(size_t)o * a.boff_stride + kl + 1] : 0;
-      if (pos < tot) en = a.ent[(size_t)o * a.CAP + pos];
-    }
-    sidx[e] = (uint16_t)en.x;
-    sw[e] = __int_as_float(en.y);
+  // ---- init: taps and bucket offsets first (small), then only the short buckets
+  // (k <= C - 1 - l0) of the block's sources, one warp per source, and the ring
+  for (int ol = tid; ol < NT; ol += NTH) {
+    const bool ok = ol < nts;
+    tl0[ol] = ok ? a.tap_l0[o0 + ol] : RING;
+    tnt[ol] = ok ? a.tap_nt[o0 + ol] : 0;
+    surg[ol] = ok && a.tap_l0[o0 + ol] <= 1;
   }
   for (int e = tid; e < NT * (K + 2); e += NTH) {
     const int ol = e / (K + 2);
@@ -114,31 +108,23 @@ __global__ void __launch_bounds__(512, 1) k_bwd_chunk(ChunkArgs a) {
     }
     sbo[e] = off;
   }
-  for (int ol = tid; ol < NT; ol += NTH) {
-    const bool ok = ol < nts;
-    tl0[ol] = ok ? a.tap_l0[o0 + ol] : RING;
-    tnt[ol] = ok ? a.tap_nt[o0 + ol] : 0;
-    surg[ol] = ok && a.tap_l0[o0 + ol] <= 1;
-  }
   for (int e = tid; e < NT * a.TAPS; e += NTH) {
     const int ol = e / a.TAPS;
     tw[e] = ol < nts ? a.tap_w[(size_t)(o0 + ol) * a.TAPS + (e % a.TAPS)] : 0.f;
   }
   for (int e = tid; e < NT * RS; e += NTH) ring[e] = 0.f;
-  for (int i = tid; i < N; i += NTH) rowq[i] = RING;
   if (tid == 0) s_abort = 0;
   __syncthreads();
-  // rowq[i]: the first chunk position q (gr(t0 + q) staged at step t0 + q) from which a
-  // short synapse of this block reads target row i: l0_o + k over the entries of bucket k
-  for (int e = tid; e < NT * a.CAPS; e += NTH) {
-    const int ol = e / a.CAPS, pos = e % a.CAPS;
-    if (ol >= nts) continue;
-    const int l0 = tl0[ol];
-    const int kl = min(K, RING - 1 - l0);
-    if (kl < 0 || pos >= sbo[ol * (K + 2) + kl + 1]) continue;
-    int k = 0;
-    while (k < kl && pos >= sbo[ol * (K + 2) + k + 1]) ++k;
-    atomicMin(&rowq[sidx[e]], l0 + k);
+  // entries past a source's short prefix are never read, so they are not loaded
+  for (int ol = warp; ol < nts; ol += NTH / 32) {
+    const int kl = min(K, RING - 1 - tl0[ol]);
+    const int tot = kl >= 0 ? sbo[ol * (K + 2) + kl + 1] : 0;
+    const int2* src = a.ent + (size_t)(o0 + ol) * a.CAP;
+    for (int pos = lane; pos < tot; pos += 32) {
+      const int2 en = src[pos];
+      sidx[(size_t)ol * a.CAPS + pos] = (uint16_t)en.x;
+      sw[(size_t)ol * a.CAPS + pos] = __int_as_float(en.y);
+    }
   }
   __syncthreads();
 
@@ -293,13 +279,10 @@ __global__ void __launch_bounds__(512, 1) k_bwd_chunk(ChunkArgs a) {
       __syncthreads();
       if (s_abort) return;
       {
-        // only the rows a short synapse of this block reads from gr(t) (position t - t0)
-        const int q = t - t0;
         const int n4 = N * BT / 4;
         const float4* xs = (const float4*)xb;
         float4* gd = (float4*)grc;
-        for (int v = tid; v < n4; v += NTH)
-          if (rowq[v >> 4] <= q) gd[v] = __ldcg(xs + v);
+        for (int v = tid; v < n4; v += NTH) gd[v] = __ldcg(xs + v);
       }
       __syncthreads();
       // ===== C2: offset 0 of a source with a lag-1 tap (read at step t - 1)
@@ -378,8 +361,10 @@ constexpr uint32_t kGzABytes = kGzRows * 64 * 2, kGzBBytes = kGzCols * 64 * 2;
 constexpr uint32_t kGzStageBytes = 2 * kGzABytes + 2 * kGzBBytes;
 constexpr size_t kGzSmem = (size_t)kGzStages * kGzStageBytes + 1024;
 
+constexpr int kGzEpiWarps = 4, kGzThreads = 64 + 32 * kGzEpiWarps;
+
 struct GzArgs {
-  int T, B, N, t0;
+  int T, B, N, t0, ntiles;
   float* gz;
   long long spin_ns;
 };
@@ -397,35 +382,44 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// One CTA: 16 samples x the chunk's 8 steps (rows b*8 + q) against 256 (source, offset)
-// columns (source-major, KP1 = K+1 offsets per source, gz_ntg(KP1) sources per tile).
+// Persistent chunk GEMM: one CTA per SM walks the output tiles (tile id = n * tiles_m + m,
+// so the CTAs of a wave share the masked-W tile of their column block through L2).
+// A tile is 16 samples x the chunk's 8 steps (rows b*8 + q) against 256 (source, offset)
+// columns (source-major, KP1 = K+1 offsets per source, gz_ntg(KP1) sources per tile);
 // A = gr pieces from the (B, T, Np) layout through a 3-D tensor map (box 64 x 8 x 16),
-// B = the offset-masked W pieces (tile rows of 256, K-major).  Two pipeline stages of all
-// four pieces of a 64-wide reduction block; per block 12 MMAs (3 products x 4 K-steps).
-// Epilogue: thread (warp w, lane l) holds row (b = 4w + l/8, q = l%8); the shift sum over
-// the offsets is a shuffle inside the 8-lane group of a sample.
+// B = the offset-masked W pieces (tile rows of 256, K-major).
+// Warp roles: warp 0 streams the four pieces of each 64-wide reduction block through a
+// two-stage ring (TMA, per-CTA loads); warp 1 issues 12 MMAs per block (3 products x 4
+// K-steps) into one of two tensor-memory accumulators (256 columns each), so the MMAs of
+// the next tile run while warps 2..5 drain the previous one; the epilogue warps read their
+// 32-lane quarter of the accumulator (thread = row (b, q)), form the shift sums over the
+// offsets with shuffles inside each sample's 8-lane group, and add them into gz.
 template <int KP1>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kGzThreads, 1)
     k_chunk_gz(const __grid_constant__ CUtensorMap mahi, const __grid_constant__ CUtensorMap malo,
                const __grid_constant__ CUtensorMap mbhi, const __grid_constant__ CUtensorMap mblo, const GzArgs g) {
   static_assert(KP1 >= 1 && KP1 <= kChunk + 1, "offset window wider than two chunks");
   constexpr int NTG = gz_ntg(KP1), USED = NTG * KP1;
   extern __shared__ unsigned char dsm[];
-  __shared__ __align__(8) uint64_t bars[2 * kGzStages + 1];
+  __shared__ __align__(8) uint64_t bars[2 * kGzStages + 4];
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t base = (smem_u32(dsm) + 1023u) & ~1023u;
-  const uint32_t full0 = smem_u32(&bars[0]), empty0 = smem_u32(&bars[kGzStages]), done = smem_u32(&bars[2 * kGzStages]);
-  const int b0 = (int)blockIdx.x * kGzSamples, n0 = (int)blockIdx.y * kGzCols, ob = (int)blockIdx.y * NTG;
+  const uint32_t full0 = smem_u32(&bars[0]), empty0 = smem_u32(&bars[kGzStages]);
+  const uint32_t accf0 = smem_u32(&bars[2 * kGzStages]), acce0 = smem_u32(&bars[2 * kGzStages + 2]);
   const int t0 = g.t0, kb = (g.N + 63) / 64;
+  const int tiles_m = (g.B + kGzSamples - 1) / kGzSamples, total = tiles_m * g.ntiles;
 
   if (tid == 0) {
     for (int s = 0; s < kGzStages; ++s) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
     }
-    mbar_init(done, 1);
+    for (int q = 0; q < 2; ++q) {
+      mbar_init(accf0 + 8 * q, 1);
+      mbar_init(acce0 + 8 * q, kGzEpiWarps);
+    }
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&mahi) : "memory");
@@ -433,7 +427,7 @@ __global__ void __launch_bounds__(128, 1)
   }
   if (warp == 2) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                 "r"((uint32_t)kGzCols)
+                 "r"((uint32_t)(2 * kGzCols))
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -443,98 +437,123 @@ __global__ void __launch_bounds__(128, 1)
   const uint32_t tmem = s_tmem;
   volatile int* abort = &s_abort;
 
-  if (warp == 0 && lane == 0) {
-    for (int j = 0; j < kb; ++j) {
-      const int s = j % kGzStages;
-      const uint32_t ph = (uint32_t)(j / kGzStages) & 1u;
-      if (!mbar_wait(empty0 + 8 * s, ph ^ 1u, g.spin_ns, abort)) break;
-      const uint32_t st = base + s * kGzStageBytes;
-      mbar_expect_tx(full0 + 8 * s, kGzStageBytes);
-      tma_load_3d(st, &mahi, j * 64, t0, b0, full0 + 8 * s);
-      tma_load_3d(st + kGzABytes, &malo, j * 64, t0, b0, full0 + 8 * s);
-      tma_load_2d(st + 2 * kGzABytes, &mbhi, j * 64, n0, full0 + 8 * s);
-      tma_load_2d(st + 2 * kGzABytes + kGzBBytes, &mblo, j * 64, n0, full0 + 8 * s);
-    }
-  } else if (warp == 1 && lane == 0) {
-    constexpr uint32_t idesc = umma_idesc_bf16(kGzCols, false, false);
-    for (int j = 0; j < kb; ++j) {
-      const int s = j % kGzStages;
-      const uint32_t ph = (uint32_t)(j / kGzStages) & 1u;
-      if (!mbar_wait(full0 + 8 * s, ph, g.spin_ns, abort)) break;
-      tc_fence_after();
-      const uint32_t st = base + s * kGzStageBytes;
-      const uint64_t ahi = umma_desc_sw128(st, false), alo = umma_desc_sw128(st + kGzABytes, false);
-      const uint64_t bhi = umma_desc_sw128(st + 2 * kGzABytes, false);
-      const uint64_t blo = umma_desc_sw128(st + 2 * kGzABytes + kGzBBytes, false);
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        umma_bf16(tmem, ahi + 2 * kk, bhi + 2 * kk, idesc, (j > 0 || kk > 0) ? 1u : 0u);
-        umma_bf16(tmem, ahi + 2 * kk, blo + 2 * kk, idesc, 1u);
-        umma_bf16(tmem, alo + 2 * kk, bhi + 2 * kk, idesc, 1u);
-      }
-      umma_commit(empty0 + 8 * s);
-    }
-    umma_commit(done);
-  }
-  __syncwarp();
-
-  const bool ok = mbar_wait(done, 0, g.spin_ns, abort);
-  __syncwarp();
-  tc_fence_after();
-  const int q = lane & 7, grp = lane & 24;
-  const int b = b0 + warp * 4 + (lane >> 3);
-  const bool brow = ok && b < g.B;
-  const size_t BN = (size_t)g.B * g.N;
-  const int s0 = t0 + q, s1 = t0 + q - kChunk;
-  // gz rows of this thread's two output steps; each group of 4 consecutive sources is one
-  // vector reduction when N is a multiple of 4 (rows 16-byte aligned), else 4 scalar ones
-  float* row0 = (brow && s0 < g.T) ? g.gz + (size_t)s0 * BN + (size_t)b * g.N : nullptr;
-  float* row1 = (brow && s1 >= 0) ? g.gz + (size_t)s1 * BN + (size_t)b * g.N : nullptr;
-  const bool vec = (g.N & 3) == 0;
-  float a0[4], a1[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) a0[i] = a1[i] = 0.f;
-#pragma unroll
-  for (int cc = 0; cc < kGzCols / 32; ++cc) {
-    if (cc * 32 >= USED) break;
-    float v[32];
-    if (ok) {
-      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(cc * 32), v);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = 0.f;
-    }
-#pragma unroll
-    for (int jj = 0; jj < 32; ++jj) {
-      const int c = cc * 32 + jj;
-      if (c < USED) {
-        const int k = c % KP1, ol = c / KP1, g4 = ol & 3;
-        const int src = q + k;   // lane of row tau = t0 + src (window 0) or t0 + src - 8
-        const float x = __shfl_sync(0xffffffffu, v[jj], grp | (src & 7));
-        if (src < kChunk) a0[g4] += x;
-        else a1[g4] += x;
-        if (k == KP1 - 1 && g4 == 3) {   // sources ol-3 .. ol complete
-          const int o = ob + ol - 3;
-          if (vec) {
-            if (row0 && o < g.N) red_add_v4(row0 + o, a0[0], a0[1], a0[2], a0[3]);
-            if (row1 && o < g.N) red_add_v4(row1 + o, a1[0], a1[1], a1[2], a1[3]);
-          } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              if (row0 && o + i < g.N) atomicAdd(row0 + o + i, a0[i]);
-              if (row1 && o + i < g.N) atomicAdd(row1 + o + i, a1[i]);
-            }
-          }
-#pragma unroll
-          for (int i = 0; i < 4; ++i) a0[i] = a1[i] = 0.f;
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      for (int tile = blockIdx.x; tile < total && !*abort; tile += gridDim.x) {
+        const int b0 = (tile % tiles_m) * kGzSamples, n0 = (tile / tiles_m) * kGzCols;
+        for (int j = 0; j < kb; ++j, ++it) {
+          const int s = it % kGzStages;
+          const uint32_t ph = (uint32_t)(it / kGzStages) & 1u;
+          if (!mbar_wait(empty0 + 8 * s, ph ^ 1u, g.spin_ns, abort)) break;
+          const uint32_t st = base + s * kGzStageBytes;
+          mbar_expect_tx(full0 + 8 * s, kGzStageBytes);
+          tma_load_3d(st, &mahi, j * 64, t0, b0, full0 + 8 * s);
+          tma_load_3d(st + kGzABytes, &malo, j * 64, t0, b0, full0 + 8 * s);
+          tma_load_2d(st + 2 * kGzABytes, &mbhi, j * 64, n0, full0 + 8 * s);
+          tma_load_2d(st + 2 * kGzABytes + kGzBBytes, &mblo, j * 64, n0, full0 + 8 * s);
         }
       }
     }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(kGzCols, false, false);
+      int it = 0, lt = 0;
+      for (int tile = blockIdx.x; tile < total && !*abort; tile += gridDim.x, ++lt) {
+        const int acc = lt & 1;
+        const uint32_t u = (uint32_t)(lt >> 1);
+        // the epilogue has drained this accumulator's previous tile
+        if (!mbar_wait(acce0 + 8 * acc, (u & 1u) ^ 1u, g.spin_ns, abort)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(acc * kGzCols);
+        bool ok = true;
+        for (int j = 0; j < kb; ++j, ++it) {
+          const int s = it % kGzStages;
+          const uint32_t ph = (uint32_t)(it / kGzStages) & 1u;
+          if (!mbar_wait(full0 + 8 * s, ph, g.spin_ns, abort)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t st = base + s * kGzStageBytes;
+          const uint64_t ahi = umma_desc_sw128(st, false), alo = umma_desc_sw128(st + kGzABytes, false);
+          const uint64_t bhi = umma_desc_sw128(st + 2 * kGzABytes, false);
+          const uint64_t blo = umma_desc_sw128(st + 2 * kGzABytes + kGzBBytes, false);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            umma_bf16(d, ahi + 2 * kk, bhi + 2 * kk, idesc, (j > 0 || kk > 0) ? 1u : 0u);
+            umma_bf16(d, ahi + 2 * kk, blo + 2 * kk, idesc, 1u);
+            umma_bf16(d, alo + 2 * kk, bhi + 2 * kk, idesc, 1u);
+          }
+          umma_commit(empty0 + 8 * s);
+        }
+        if (!ok) break;
+        umma_commit(accf0 + 8 * acc);   // arrives once this tile's MMAs have completed
+      }
+    }
+  } else {
+    // ---- epilogue warps 2..5: TMEM lane quarter qd = warp % 4 holds rows 32 qd + lane
+    const int qd = warp & 3;
+    const int q = lane & 7, grp = lane & 24;
+    const size_t BN = (size_t)g.B * g.N;
+    const bool vec = (g.N & 3) == 0;
+    const int s0 = t0 + q, s1 = t0 + q - kChunk;
+    int lt = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++lt) {
+      const int acc = lt & 1;
+      const uint32_t u = (uint32_t)(lt >> 1);
+      const int b0 = (tile % tiles_m) * kGzSamples, ob = (tile / tiles_m) * NTG;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(accf0 + 8 * acc, u & 1u, g.spin_ns, abort));
+      if (!ok) break;
+      tc_fence_after();
+      const int b = b0 + qd * 4 + (lane >> 3);
+      const bool brow = b < g.B;
+      float* row0 = (brow && s0 < g.T) ? g.gz + (size_t)s0 * BN + (size_t)b * g.N : nullptr;
+      float* row1 = (brow && s1 >= 0) ? g.gz + (size_t)s1 * BN + (size_t)b * g.N : nullptr;
+      float a0[4], a1[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a0[i] = a1[i] = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < kGzCols / 32; ++cc) {
+        if (cc * 32 >= USED) break;
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(qd * 32) << 16) + (uint32_t)(acc * kGzCols + cc * 32), v);
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          const int c = cc * 32 + jj;
+          if (c < USED) {
+            const int k = c % KP1, ol = c / KP1, g4 = ol & 3;
+            const int src = q + k;   // lane of row tau = t0 + src (window 0) or t0 + src - 8
+            const float x = __shfl_sync(0xffffffffu, v[jj], grp | (src & 7));
+            if (src < kChunk) a0[g4] += x;
+            else a1[g4] += x;
+            if (k == KP1 - 1 && g4 == 3) {   // sources ol-3 .. ol complete
+              const int o = ob + ol - 3;
+              if (vec) {
+                if (row0 && o < g.N) red_add_v4(row0 + o, a0[0], a0[1], a0[2], a0[3]);
+                if (row1 && o < g.N) red_add_v4(row1 + o, a1[0], a1[1], a1[2], a1[3]);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  if (row0 && o + i < g.N) atomicAdd(row0 + o + i, a0[i]);
+                  if (row1 && o + i < g.N) atomicAdd(row1 + o + i, a1[i]);
+                }
+              }
+#pragma unroll
+              for (int i = 0; i < 4; ++i) a0[i] = a1[i] = 0.f;
+            }
+          }
+        }
+      }
+      // the accumulator's reads are complete: hand it back to the MMA warp
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(acce0 + 8 * acc) : "memory");
+    }
   }
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == 2)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)kGzCols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(2 * kGzCols))
+                 : "memory");
 }
 
 // Offset-masked W as the GEMM's B operand: row r = tile * 256 + c, c = ol * KP1 + k
