@@ -259,7 +259,9 @@ int delrec_scan_time_part(int part, double* total_ms, int* launches);
 /* Reverse-scan variant of the layer backwards (process-wide).  0 (default): hybrid layers
  * whose shape allows it run the chunked scan -- the delayed-gradient contraction of every
  * synapse whose lag reaches past the current 8-step chunk as one tensor-core GEMM per
- * chunk, the short-lag synapses step by step; 1: the step-by-step scans only.  Both give
+ * chunk, the short-lag synapses step by step in blocks that own whole samples; 1: the
+ * step-by-step scans only; 2: the chunked scan with its steps split over source slices
+ * that exchange gr through L2 every step (kept for comparison).  All give
  * the reference's gradients within the library's tolerance; the workspace size queries
  * cover either variant.  Replaces no reference call (the reference has one Triton
  * kernel per layer kind, triton_kernels/synaptic_eventdriven.py:323-364). */

@@ -16,6 +16,7 @@
 #include "backward_hybrid64.cuh"
 #include "backward_axonal_mma.cuh"
 #include "backward_chunk.cuh"
+#include "backward_chunk_local.cuh"
 #include "dense.cuh"
 #include "forward.cuh"
 #include "gemm_tc.cuh"
@@ -965,8 +966,9 @@ static int run_axstep(const delrec_layer* ly, const delrec_lif* lif, const float
 }
 
 // ---- chunked reverse scan (backward_chunk.cuh) ----------------------------------------
-// 0: hybrid layers run the chunked scan where the shape allows it; 1: every layer runs the
-// step-by-step scans (delrec_set_reverse_scan).
+// 0: hybrid layers run the chunked scan where the shape allows it, its steps in the
+// sample-local form; 1: every layer runs the step-by-step scans; 2: the chunked scan with
+// the steps exchanging gr between blocks (delrec_set_reverse_scan).
 static std::atomic<int> g_reverse_scan{0};
 
 struct ChunkPlan {
@@ -997,6 +999,13 @@ static size_t chunk_ws(const delrec_layer* ly, const ChunkPlan& cp) {
   c.take<__nv_bfloat16>((size_t)cp.ntiles * kGzCols * cp.Np);   // masked W pieces
   c.take<__nv_bfloat16>((size_t)cp.ntiles * kGzCols * cp.Np);
   c.take<float>((size_t)ly->B * ly->N);                       // LIF carry between chunks
+  c.take<uint16_t>((size_t)ly->N * plan_backward(ly, DELREC_HYBRID).CAP);   // short entries
+  c.take<float>((size_t)ly->N * plan_backward(ly, DELREC_HYBRID).CAP);
+  const int ecap = loc_entry_cap(kSmemLimit, loc_smem_plan(ly->N, plan_backward(ly, DELREC_HYBRID).TAPS));
+  c.take<uint16_t>((size_t)std::max(ecap, 8));                // compact cache
+  c.take<float>((size_t)std::max(ecap, 8));
+  c.take<int4>((size_t)ly->N * kChunk);                       // (source, bucket) pairs
+  c.take<int>(16);                                            // pair counts, meta
   return c.off;
 }
 
@@ -1052,6 +1061,15 @@ static int run_chunked(const delrec_layer* ly, const Hyb64Plan& h64, const Chunk
   __nv_bfloat16* wm_hi = c.take<__nv_bfloat16>(wrows * Np);
   __nv_bfloat16* wm_lo = c.take<__nv_bfloat16>(wrows * Np);
   float* lam = c.take<float>((size_t)B * N);
+  uint16_t* sh_idx = c.take<uint16_t>((size_t)N * h64.CAP);
+  float* sh_w = c.take<float>((size_t)N * h64.CAP);
+  const LocSmem lplan = loc_smem_plan(N, base.TAPS);
+  const size_t lsmem = kSmemLimit;   // the fixed part, the rest caches the short entries
+  const int lecap = loc_entry_cap(lsmem, lplan);
+  uint16_t* c_idx = c.take<uint16_t>((size_t)std::max(lecap, 8));
+  float* c_w = c.take<float>((size_t)std::max(lecap, 8));
+  int4* pairs = c.take<int4>((size_t)N * kChunk);
+  int* pcnt = c.take<int>(16);
   if (!c.ok) return DELREC_ERR_WORKSPACE;
   k_mask_w<<<grid_for(wrows * Np, 256), 256, 0, st>>>(N, Np, cp.KP1, (int)wrows, W, offT, wm_hi, wm_lo);
   DR_LAUNCHED();
@@ -1061,12 +1079,30 @@ static int run_chunked(const delrec_layer* ly, const Hyb64Plan& h64, const Chunk
       !tmap_bf16(&maps[2], wm_hi, N, (long long)wrows, Np, kGzCols) ||
       !tmap_bf16(&maps[3], wm_lo, N, (long long)wrows, Np, kGzCols))
     return DELREC_ERR_ARG;
+  // steps: the sample-local kernel (no exchange) unless the exchange form is selected
+  const bool local = g_reverse_scan.load() != 2;
+  const int lppt = cdiv(kLocS * N, kLocThreads);
   auto kern = k_bwd_chunk<kH64Taps>;
-  int rc = set_smem(kern, cp.smem);
-  if (rc) return rc;
-  int per_sm = 0;
-  DR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kH64Threads, cp.smem));
-  if (per_sm < 1 || h64.CS * h64.tiles > per_sm * kSMs) return DELREC_ERR_UNSUPPORTED;
+  auto lkern = lppt <= 1 ? k_bwd_chunk_local<kH64Taps, 1>
+                         : (lppt <= 2 ? k_bwd_chunk_local<kH64Taps, 2> : k_bwd_chunk_local<kH64Taps, 4>);
+  int rc = DELREC_OK;
+  if (local) {
+    if (lppt > 4 || lplan.fixed + 512 > lsmem) return DELREC_ERR_UNSUPPORTED;
+    rc = set_smem(lkern, lsmem);
+    if (rc) return rc;
+    k_short_entries<<<N, 64, 0, st>>>(N, h64.K, h64.CAP, base.boff_stride, base.ent, base.boff, base.tap_l0, sh_idx,
+                                      sh_w);
+    DR_LAUNCHED();
+    k_short_pairs<<<1, kLocThreads, 0, st>>>(N, h64.K, h64.CAP, base.boff_stride, base.boff, base.tap_l0, sh_idx, sh_w,
+                                             lecap, c_idx, c_w, pairs, pcnt, pcnt + 8);
+    DR_LAUNCHED();
+  } else {
+    rc = set_smem(kern, cp.smem);
+    if (rc) return rc;
+    int per_sm = 0;
+    DR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kH64Threads, cp.smem));
+    if (per_sm < 1 || h64.CS * h64.tiles > per_sm * kSMs) return DELREC_ERR_UNSUPPORTED;
+  }
   ChunkArgs a{};
   a.T = T; a.B = B; a.N = N; a.K = h64.K; a.CS = h64.CS; a.NT = h64.NT; a.TAPS = base.TAPS;
   a.CAPS = h64.CAPS; a.CAP = h64.CAP; a.boff_stride = base.boff_stride;
@@ -1082,11 +1118,17 @@ static int run_chunked(const delrec_layer* ly, const Hyb64Plan& h64, const Chunk
     a.t0 = ch * kChunk;
     a.t_hi = std::min(T - 1, a.t0 + kChunk - 1);
     a.arr_base = (unsigned int)((T - 1 - a.t_hi) * h64.CS);
-    ChunkArgs ac = a;
-    void* args[] = {(void*)&ac};
     scan_mark(0, st, 1);
-    DR_CUDA(cudaLaunchCooperativeKernel((const void*)kern, dim3(h64.CS * h64.tiles), dim3(kH64Threads), args,
-                                        cp.smem, st));
+    if (local) {
+      LocArgs la{a, sh_idx, sh_w, c_idx, c_w, pairs, pcnt, pcnt + 8, lecap};
+      lkern<<<cdiv(B, kLocS), kLocThreads, lsmem, st>>>(la);
+      DR_CUDA(cudaGetLastError());
+    } else {
+      ChunkArgs ac = a;
+      void* args[] = {(void*)&ac};
+      DR_CUDA(cudaLaunchCooperativeKernel((const void*)kern, dim3(h64.CS * h64.tiles), dim3(kH64Threads), args,
+                                          cp.smem, st));
+    }
     scan_mark(1, st, 1);
     ++g_launches;
     g.t0 = a.t0;
@@ -1471,7 +1513,7 @@ int delrec_exchange_floor(const delrec_layer* ly, void* ws, size_t wsb, void* st
 }
 
 int delrec_set_reverse_scan(int variant) {
-  if (variant != 0 && variant != 1) return DELREC_ERR_ARG;
+  if (variant < 0 || variant > 2) return DELREC_ERR_ARG;
   g_reverse_scan.store(variant);
   return DELREC_OK;
 }

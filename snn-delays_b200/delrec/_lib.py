@@ -180,7 +180,7 @@ def scan_time(part=0):
     return ms.value, n.value
 
 
-REVERSE_SCAN_CHUNKED, REVERSE_SCAN_STEPWISE = 0, 1
+REVERSE_SCAN_CHUNKED, REVERSE_SCAN_STEPWISE, REVERSE_SCAN_CHUNKED_EXCHANGE = 0, 1, 2
 
 
 def set_reverse_scan(variant: int):

@@ -110,21 +110,23 @@ def test_random_vs_oracle(shape):
 @pytest.mark.parametrize("T,B,N,K,sigma", [(64, 256, 512, 8, 0.0), (45, 130, 264, 5, 1.0), (16, 40, 96, 8, 0.0)])
 def test_chunked_reverse_scan_matches_stepwise(T, B, N, K, sigma):
     """The chunked reverse scan (tensor-core GEMM per 8-step chunk for the long-lag
-    synapses) and the step-by-step scan on the same hybrid layer: the forward is shared, so
-    the spikes are identical, and every gradient agrees within the parity tolerance."""
+    synapses; its steps sample-local or exchanging gr between source slices) and the
+    step-by-step scan on the same hybrid layer: the forward is shared, so the spikes are
+    identical, and every gradient agrees within the parity tolerance."""
     from delrec import _lib
     case = _random_case("hybrid", 900 + N, T, B, N, sigma, False, True, True, 25.0, K)
     outs = []
-    for variant in (_lib.REVERSE_SCAN_CHUNKED, _lib.REVERSE_SCAN_STEPWISE):
+    for variant in (_lib.REVERSE_SCAN_CHUNKED, _lib.REVERSE_SCAN_STEPWISE, _lib.REVERSE_SCAN_CHUNKED_EXCHANGE):
         _lib.set_reverse_scan(variant)
         try:
             outs.append(run_cuda(case["meta"], case["inputs"]))
         finally:
             _lib.set_reverse_scan(_lib.REVERSE_SCAN_CHUNKED)
-    a, b = outs
-    assert torch.equal(a["y"], b["y"])
-    for k in ("dx", "dW", "dd", "dbias"):
-        assert rel_err(a[k], b[k]) < 1e-4, k
+    a = outs[0]
+    for b in outs[1:]:
+        assert torch.equal(a["y"], b["y"])
+        for k in ("dx", "dW", "dd", "dbias"):
+            assert rel_err(a[k], b[k]) < 1e-4, k
     assert _lib.status() == 0
 
 
