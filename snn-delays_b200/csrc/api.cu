@@ -386,6 +386,7 @@ static BwdPlan plan_backward(const delrec_layer* ly, int kind) {
   best.PADM = best.ok ? 4 * (32 / best.BT) : 4;
   // room for the padding of either backward kernel (the specialised hybrid one pads to 8)
   best.CAP = (mode == 1 ? N : N * std::min(ly->L, 2 * kTapsMax)) + best.NKEY * std::max(best.PADM, 8);
+  best.CAP = (best.CAP + 7) / 8 * 8;   // rows start 16-byte aligned for 8-byte entries (4-entry vectors)
   return best;
 }
 
@@ -1081,10 +1082,13 @@ static int run_chunked(const delrec_layer* ly, const Hyb64Plan& h64, const Chunk
     return DELREC_ERR_ARG;
   // steps: the sample-local kernel (no exchange) unless the exchange form is selected
   const bool local = g_reverse_scan.load() != 2;
-  const int lppt = cdiv(kLocS * N, kLocThreads);
+  // one (sample, source) pair per thread where it fits in a block of 1024, else 512 threads
+  const int lnth = kLocS * N <= 1024 ? 1024 : kLocThreads;
+  const int lppt = cdiv(kLocS * N, lnth);
   auto kern = k_bwd_chunk<kH64Taps>;
-  auto lkern = lppt <= 1 ? k_bwd_chunk_local<kH64Taps, 1>
-                         : (lppt <= 2 ? k_bwd_chunk_local<kH64Taps, 2> : k_bwd_chunk_local<kH64Taps, 4>);
+  auto lkern = lnth == 1024 ? k_bwd_chunk_local<kH64Taps, 1, 1024>
+                            : (lppt <= 2 ? k_bwd_chunk_local<kH64Taps, 2, kLocThreads>
+                                         : k_bwd_chunk_local<kH64Taps, 4, kLocThreads>);
   int rc = DELREC_OK;
   if (local) {
     if (lppt > 4 || lplan.fixed + 512 > lsmem) return DELREC_ERR_UNSUPPORTED;
@@ -1121,7 +1125,7 @@ static int run_chunked(const delrec_layer* ly, const Hyb64Plan& h64, const Chunk
     scan_mark(0, st, 1);
     if (local) {
       LocArgs la{a, sh_idx, sh_w, c_idx, c_w, pairs, pcnt, pcnt + 8, lecap};
-      lkern<<<cdiv(B, kLocS), kLocThreads, lsmem, st>>>(la);
+      lkern<<<cdiv(B, kLocS), lnth, lsmem, st>>>(la);
       DR_CUDA(cudaGetLastError());
     } else {
       ChunkArgs ac = a;

@@ -197,11 +197,11 @@ struct LocArgs {
   int ecap;                // entries the block's shared-memory cache holds
 };
 
-template <int TPF, int PPT>
-__global__ void __launch_bounds__(kLocThreads, 1) k_bwd_chunk_local(LocArgs la) {
+template <int TPF, int PPT, int NTH>
+__global__ void __launch_bounds__(NTH, 1) k_bwd_chunk_local(LocArgs la) {
   extern __shared__ __align__(16) unsigned char smem[];
   const ChunkArgs& a = la.c;
-  constexpr int S = kLocS, NTH = kLocThreads, RING = kChunk, G = kLocGroup;
+  constexpr int S = kLocS, RING = kChunk, G = kLocGroup;
   const int N = a.N, T = a.T, B = a.B, TAPS = a.TAPS, tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
   const int b0 = (int)blockIdx.x * S;
@@ -346,11 +346,18 @@ __global__ void __launch_bounds__(kLocThreads, 1) k_bwd_chunk_local(LocArgs la) 
       float acc[S];
 #pragma unroll
       for (int s2 = 0; s2 < S; ++s2) acc[s2] = 0.f;
-      for (int e = pr.y + gl; e < pr.z; e += G) {
-        const int i = ix[e];
-        const float w = wv[e];
+      // 4 consecutive entries per lane (bucket bounds and cache offsets are multiples of 8)
+      for (int e = pr.y + 4 * gl; e < pr.z; e += 4 * G) {
+        const ushort4 i4 = *(const ushort4*)(ix + e);
+        const float4 w4 = *(const float4*)(wv + e);
 #pragma unroll
-        for (int s2 = 0; s2 < S; ++s2) acc[s2] = fmaf(w, grs[s2 * N + i], acc[s2]);
+        for (int s2 = 0; s2 < S; ++s2) {
+          const float* gs = grs + s2 * N;
+          acc[s2] = fmaf(w4.x, gs[i4.x], acc[s2]);
+          acc[s2] = fmaf(w4.y, gs[i4.y], acc[s2]);
+          acc[s2] = fmaf(w4.z, gs[i4.z], acc[s2]);
+          acc[s2] = fmaf(w4.w, gs[i4.w], acc[s2]);
+        }
       }
 #pragma unroll
       for (int s2 = 0; s2 < S; ++s2) {
