@@ -4,7 +4,8 @@ Workload (the north-star model): SNN_recurrent_hybrid_delays 
 recurrent hybrid-delay LIF layers of 512 neurons (learned axonal base U[0,25] + frozen
 integer offsets U{0..8}, sigma = 0), 700 input channels of Bernoulli spikes with
 per-channel rates U[0, 5%], T = 250, 35 classes, batch 256 per GPU.  One step = forward,
-time-summed cross-entropy, backward, gradient all-reduce (N > 1) and an Adam update.
+time-summed cross-entropy, backward with the gradient all-reduce of N > 1 ranks
+(bucketed, launched during the backward) and an Adam update.
 Synthetic data stands in for the SSC-shaped dataset (not available offline).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
@@ -193,10 +194,18 @@ def dist_setup(n_gpus):
     return 0, 1, 0
 
 
-def allreduce_grads(params, ws):
+def make_allreduce(params, ws):
+    """The gradient averaging of N > 1 ranks: bucketed all-reduces launched from the
+    gradient hooks during the backward (they overlap the earlier layers' backward)."""
+    if ws == 1:
+        return None
+    from delrec.data_parallel import OverlappedAllReduce
+    return OverlappedAllReduce(params, bucket_bytes=2 << 20)
+
+
+def finish_allreduce(ar, params, ws):
     if ws > 1:
-        from delrec.data_parallel import allreduce_gradients
-        allreduce_gradients(params)
+        ar.finish()
 
 
 def barrier(ws):
@@ -402,6 +411,7 @@ def main():
     model, cfg = build_model(spec, B, dev)
     params = [p for p in model.parameters() if p.requires_grad]
     opt = torch.optim.Adam(params, lr=1e-3)
+    ar = make_allreduce(params, ws)
     x_cpu, labels_cpu = make_inputs(spec, B, seed=1 + rank)
     x = x_cpu.to(dev)
     labels = labels_cpu.to(dev)
@@ -411,7 +421,7 @@ def main():
         out = model(xb)
         loss = loss_fn(out, lb)
         loss.backward()
-        allreduce_grads(params, ws)
+        finish_allreduce(ar, params, ws)
         opt.step()
         model.clamp_delays()
         return loss
@@ -504,6 +514,7 @@ def main():
         model_s, _ = build_model(spec, Bs, dev)
         params_s = [p for p in model_s.parameters() if p.requires_grad]
         opt_s = torch.optim.Adam(params_s, lr=1e-3)
+        ar_s = make_allreduce(params_s, ws)
         xs = x[:, :Bs].contiguous()
         ls = labels[:Bs].contiguous()
 
@@ -511,7 +522,7 @@ def main():
             opt_s.zero_grad(set_to_none=True)
             loss = loss_fn(model_s(xb), lb)
             loss.backward()
-            allreduce_grads(params_s, ws)
+            finish_allreduce(ar_s, params_s, ws)
             opt_s.step()
             model_s.clamp_delays()
             return loss
@@ -618,7 +629,7 @@ def roofline_probe(model, step, x, labels, spec, B):
     peak = peaks["bf16_tflops_sustained"] / 3.0
     achieved = flops / (ms / 1e3) / 1e12
     chunked = n_gemm > 0
-    per_unit = _profiled_traffic("k_bwd_chunk" if chunked else "k_bwd_hybrid64") \
+    per_unit = _profiled_traffic("k_bwd_chunk_cfg4" if chunked else "k_bwd_hybrid64") \
         if spec["model"].endswith("hybrid_delays") else None
     kern = {"hybrid": "k_bwd_chunk steps + k_chunk_gz tensor-core chunk GEMMs" if chunked else "k_bwd_hybrid64",
             "synaptic": "k_bwd_hybrid64 (synaptic buckets)", "axonal": "k_bwd_axonal_mma or k_bwd (by size)"}
@@ -629,8 +640,8 @@ def roofline_probe(model, step, x, labels, spec, B):
            "ms_per_launch": ms, "launches_timed": n, "flops_per_launch": flops,
            "flops_definition": "2*N^2*B*T: the recurrent contraction gz = W^T gr, each synapse once",
            "peak_source": f"bf16_tflops_sustained / 3 ({src}; fp32-accurate 3-product bf16 rate)",
-           "traffic_source": "ncu dram bytes per sample-timestep of a small-T capture, scaled to B*T"
-                             if per_unit else None}
+           "traffic_source": "ncu dram bytes per sample-timestep of a T=64 capture of the same kernels "
+                             "(profiles/), scaled to B*T" if per_unit else None}
     if chunked:
         # the chunk GEMMs: executed tensor-core work (every tile's 128x256 MMAs, three bf16
         # products over the N-target reduction) against the measured sustained bf16 rate
