@@ -1086,7 +1086,9 @@ static int run_chunked(const delrec_layer* ly, const Hyb64Plan& h64, const Chunk
   const int lnth = kLocS * N <= 1024 ? 1024 : kLocThreads;
   const int lppt = cdiv(kLocS * N, lnth);
   auto kern = k_bwd_chunk<kH64Taps>;
-  auto lkern = lnth == 1024 ? k_bwd_chunk_local<kH64Taps, 1, 1024>
+  // taps per source: the integer lags inside one triangle, at most 2*ceil(s_max) + 1
+  const bool tap4 = 2 * (int)ceilf(ly->s_max) + 1 <= 4;
+  auto lkern = lnth == 1024 ? (tap4 ? k_bwd_chunk_local<4, 1, 1024> : k_bwd_chunk_local<kH64Taps, 1, 1024>)
                             : (lppt <= 2 ? k_bwd_chunk_local<kH64Taps, 2, kLocThreads>
                                          : k_bwd_chunk_local<kH64Taps, 4, kLocThreads>);
   int rc = DELREC_OK;

@@ -21,6 +21,7 @@
 namespace delrec {
 
 constexpr int kLocS = 2, kLocThreads = 512, kLocGroup = 8;   // lanes per (source, bucket) pair
+constexpr int kLocPairCache = 1024;   // pairs staged in shared memory (the rest read from global)
 
 // The short prefix of every source's bucket list (buckets k <= min(K, 7 - l0)) split into
 // 16-bit targets and fp32 weights (6 bytes per entry, same row layout as `ent`).
@@ -42,7 +43,7 @@ __global__ void k_short_entries(int N, int K, int CAP, int boff_stride, const in
 // contributions, gr(t) of the block's samples, the pair counts per chunk position; the
 // rest caches the short entries of the smallest lags.
 struct LocSmem {
-  size_t taps, ring, grs, cnt, fixed;
+  size_t taps, ring, grs, cnt, pairs, fixed;
 };
 __host__ __device__ inline LocSmem loc_smem_plan(int N, int TAPS) {
   LocSmem p;
@@ -50,7 +51,8 @@ __host__ __device__ inline LocSmem loc_smem_plan(int N, int TAPS) {
   p.ring = align256((size_t)N * kChunk * kLocS * 4);            // [N][8][S]
   p.grs = align256((size_t)kLocS * N * 4);                      // gr(t) [S][N]
   p.cnt = 256;                                                  // pairs with lag <= q
-  p.fixed = p.taps + p.ring + p.grs + p.cnt;
+  p.pairs = (size_t)kLocPairCache * 16;                        // the first (source, bucket) pairs
+  p.fixed = p.taps + p.ring + p.grs + p.cnt + p.pairs;
   return p;
 }
 // entries (6 bytes each) the shared-memory cache of a block with `smem` bytes holds
@@ -101,7 +103,8 @@ __global__ void __launch_bounds__(kLocThreads, 1)
                   const float* __restrict__ sw, int ecap, uint16_t* __restrict__ cidx, float* __restrict__ cw,
                   int4* __restrict__ pairs, int* __restrict__ cnt, int* __restrict__ meta) {
   __shared__ int s_ent[kChunk], s_pair[kChunk], s_scan[17], s_lam;
-  const int tid = threadIdx.x;
+  __shared__ int s_cum[1024 + 1];   // cache offset of each source (N <= 1024)
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid < kChunk) s_ent[tid] = s_pair[tid] = 0;
   __syncthreads();
   for (int o = tid; o < N; o += kLocThreads) {
@@ -135,11 +138,18 @@ __global__ void __launch_bounds__(kLocThreads, 1)
     }
     int total;
     const int at = carry + loc_block_exscan(len, s_scan, &total);
-    for (int pos = 0; pos < len; ++pos) {
+    if (o < N) s_cum[o] = at;
+    carry += total;
+  }
+  if (tid == 0) s_cum[min(N, 1024)] = carry;
+  __syncthreads();
+  // one warp per source copies its cached prefix
+  for (int o = warp; o < N; o += kLocThreads / 32) {
+    const int at = s_cum[o], len = s_cum[o + 1] - at;
+    for (int pos = lane; pos < len; pos += 32) {
       cidx[at + pos] = sidx[(size_t)o * CAP + pos];
       cw[at + pos] = sw[(size_t)o * CAP + pos];
     }
-    carry += total;
   }
   if (tid == 0) {
     meta[0] = lam_s;
@@ -216,6 +226,7 @@ __global__ void __launch_bounds__(NTH, 1) k_bwd_chunk_local(LocArgs la) {
   float* ring = (float*)(smem + P.taps);                   // [N][RING][S]
   float* grs = (float*)(smem + P.taps + P.ring);           // [S][N]
   int* scnt = (int*)(smem + P.taps + P.ring + P.grs);      // [RING]
+  int4* spairs = (int4*)(smem + P.taps + P.ring + P.grs + P.cnt);   // [cnt[RING-1]]
   uint16_t* cidx = (uint16_t*)(smem + P.fixed);            // [ecap] cached targets
   float* cw = (float*)(smem + P.fixed + align256((size_t)la.ecap * 2));   // [ecap] cached weights
 
@@ -226,6 +237,7 @@ __global__ void __launch_bounds__(NTH, 1) k_bwd_chunk_local(LocArgs la) {
   for (int e = tid; e < N * TAPS; e += NTH) tw[e] = a.tap_w[e];
   for (int e = tid; e < N * RING * S; e += NTH) ring[e] = 0.f;
   if (tid < RING) scnt[tid] = la.cnt[tid];
+  for (int j = tid; j < min(la.cnt[RING - 1], kLocPairCache); j += NTH) spairs[j] = la.pairs[j];
   {
     // the compact cache (16-byte pieces; its size is a multiple of 8 entries)
     const int ncached = min(la.meta[1], la.ecap);
@@ -303,7 +315,7 @@ __global__ void __launch_bounds__(NTH, 1) k_bwd_chunk_local(LocArgs la) {
       if (bl >= S) continue;
       float grv = 0.f;
       if (pok[k]) {
-        const int lo = tl0[o], n = tnt[o];   // n <= TAPS <= TPF (checked by the planner)
+        const int lo = tl0[o], n = tnt[o];   // n <= 2*ceil(s_max)+1 <= TPF (checked by the planner)
         const float* rrow = ring + (size_t)o * RING * S + bl;
         float gfut = 0.f;
 #pragma unroll
@@ -340,7 +352,7 @@ __global__ void __launch_bounds__(NTH, 1) k_bwd_chunk_local(LocArgs la) {
       const int j = base + g;
       const bool act = j < np;
       int4 pr = make_int4(0, 0, 0, 0);
-      if (act) pr = la.pairs[j];
+      if (act) pr = j < kLocPairCache ? spairs[j] : la.pairs[j];
       const uint16_t* ix = pr.w ? cidx : la.sidx;
       const float* wv = pr.w ? cw : la.sw;
       float acc[S];
