@@ -1688,7 +1688,7 @@ int delrec_dcls_backward(int T, int B, int Cin, int Cout, int groups, int K, int
     DR_LAUNCHED();
   }
   if (dbias) {
-    k_dcls_dbias<<<cdiv(Cout, 128), 128, 0, st>>>(T * B, Cout, gout, dbias);
+    k_dcls_dbias<<<cdiv(Cout, 32), 1024, 0, st>>>(T * B, Cout, gout, dbias);
     DR_LAUNCHED();
   }
   return DELREC_OK;

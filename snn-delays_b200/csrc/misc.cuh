@@ -170,13 +170,26 @@ __global__ void k_dcls_params(int rows, int K, const float* __restrict__ w, cons
   if (dSIG) dSIG[r] = w[r] * dsg * (SIG[r] > 0.f ? 1.f : (SIG[r] < 0.f ? -1.f : 0.f));
 }
 
-// db[co] = sum_{t,b} gout[t,b,co]
-__global__ void k_dcls_dbias(int TB, int Cout, const float* __restrict__ gout, float* __restrict__ db) {
-  const int co = blockIdx.x * blockDim.x + threadIdx.x;
-  if (co >= Cout) return;
+// db[co] = sum_{t,b} gout[t,b,co]: a block of 32 warps per 32 output columns (lane =
+// column, coalesced rows); warp w sums rows w, w+32, ...; the 32 warp partials are added
+// in a fixed order (deterministic)
+__global__ void __launch_bounds__(1024) k_dcls_dbias(int TB, int Cout, const float* __restrict__ gout,
+                                                     float* __restrict__ db) {
+  __shared__ float part[32][33];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int co = blockIdx.x * 32 + lane;
   float v = 0.f;
-  for (int e = 0; e < TB; ++e) v += gout[(size_t)e * Cout + co];
-  db[co] = v;
+  if (co < Cout) {
+#pragma unroll 8
+    for (int e = w; e < TB; e += 32) v += gout[(size_t)e * Cout + co];
+  }
+  part[w][lane] = v;
+  __syncthreads();
+  if (w == 0) {
+    float sum = 0.f;
+    for (int k = 0; k < 32; ++k) sum += part[k][lane];
+    if (co < Cout) db[co] = sum;
+  }
 }
 
 }  // namespace delrec
