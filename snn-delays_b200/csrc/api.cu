@@ -973,23 +973,30 @@ static int run_axstep(const delrec_layer* ly, const delrec_lif* lif, const float
 static std::atomic<int> g_reverse_scan{0};
 
 struct ChunkPlan {
-  bool ok;
-  int KP1, ntiles, nchunks, Np;
-  size_t smem;
+  bool ok, exch;     // ok: the sample-local chunked scan applies; exch: so does its exchange form
+  int KP1, ntiles, nchunks, Np, S;
+  size_t smem;       // exchange form's step kernel
 };
-// Shape test only (the workspace query does not depend on the selected variant): a
-// hybrid layer that the 64-sample scan takes, offsets within two chunks (K + 1 <= 9).
+// Shape test only (the workspace query does not depend on the selected variant): a hybrid
+// layer whose base taps are all at lag >= 1, offsets within two chunks (K + 1 <= 9), at
+// most 8 taps per source, N <= 1024.  The exchange form also needs the 64-sample tiling.
+// S: samples per step block, 1 while the batch fills at most one wave of blocks.
 static ChunkPlan plan_chunk(const delrec_layer* ly, const BwdPlan& bp, const Hyb64Plan& h64) {
   ChunkPlan c{};
-  c.ok = false;
-  if (!h64.ok || ly->kind != DELREC_HYBRID) return c;
-  c.KP1 = h64.K + 1;
+  c.ok = c.exch = false;
+  if (ly->kind != DELREC_HYBRID || !bp.ok || bp.MM != 0 || ly->N > 1024) return c;
+  c.KP1 = ly->K + 1;
   if (c.KP1 > kChunk + 1 || bp.TAPS > kH64Taps) return c;
   c.ntiles = cdiv(ly->N, gz_ntg(c.KP1));
   c.nchunks = cdiv(ly->T, kChunk);
   c.Np = pad8(ly->N);
-  c.smem = hyb64_smem_plan(ly->N, h64.NT, h64.CAPS, h64.K, bp.TAPS, kChunk).total;
-  c.ok = c.smem <= kSmemLimit;
+  c.S = ly->B <= kSMs ? 1 : kLocSMax;
+  if (loc_smem_plan(ly->N, bp.TAPS, c.S).fixed + 512 > kSmemLimit) return c;
+  c.ok = true;
+  if (h64.ok) {
+    c.smem = hyb64_smem_plan(ly->N, h64.NT, h64.CAPS, h64.K, bp.TAPS, kChunk).total;
+    c.exch = c.smem <= kSmemLimit;
+  }
   return c;
 }
 static size_t chunk_ws(const delrec_layer* ly, const ChunkPlan& cp) {
@@ -1002,7 +1009,7 @@ static size_t chunk_ws(const delrec_layer* ly, const ChunkPlan& cp) {
   c.take<float>((size_t)ly->B * ly->N);                       // LIF carry between chunks
   c.take<uint16_t>((size_t)ly->N * plan_backward(ly, DELREC_HYBRID).CAP);   // short entries
   c.take<float>((size_t)ly->N * plan_backward(ly, DELREC_HYBRID).CAP);
-  const int ecap = loc_entry_cap(kSmemLimit, loc_smem_plan(ly->N, plan_backward(ly, DELREC_HYBRID).TAPS));
+  const int ecap = loc_entry_cap(kSmemLimit, loc_smem_plan(ly->N, plan_backward(ly, DELREC_HYBRID).TAPS, cp.S));
   c.take<uint16_t>((size_t)std::max(ecap, 8));                // compact cache
   c.take<float>((size_t)std::max(ecap, 8));
   c.take<int4>((size_t)ly->N * kChunk);                       // (source, bucket) pairs
@@ -1062,9 +1069,9 @@ static int run_chunked(const delrec_layer* ly, const Hyb64Plan& h64, const Chunk
   __nv_bfloat16* wm_hi = c.take<__nv_bfloat16>(wrows * Np);
   __nv_bfloat16* wm_lo = c.take<__nv_bfloat16>(wrows * Np);
   float* lam = c.take<float>((size_t)B * N);
-  uint16_t* sh_idx = c.take<uint16_t>((size_t)N * h64.CAP);
-  float* sh_w = c.take<float>((size_t)N * h64.CAP);
-  const LocSmem lplan = loc_smem_plan(N, base.TAPS);
+  uint16_t* sh_idx = c.take<uint16_t>((size_t)N * base.CAP);
+  float* sh_w = c.take<float>((size_t)N * base.CAP);
+  const LocSmem lplan = loc_smem_plan(N, base.TAPS, cp.S);
   const size_t lsmem = kSmemLimit;   // the fixed part, the rest caches the short entries
   const int lecap = loc_entry_cap(lsmem, lplan);
   uint16_t* c_idx = c.take<uint16_t>((size_t)std::max(lecap, 8));
@@ -1081,25 +1088,28 @@ static int run_chunked(const delrec_layer* ly, const Hyb64Plan& h64, const Chunk
       !tmap_bf16(&maps[3], wm_lo, N, (long long)wrows, Np, kGzCols))
     return DELREC_ERR_ARG;
   // steps: the sample-local kernel (no exchange) unless the exchange form is selected
-  const bool local = g_reverse_scan.load() != 2;
+  const bool local = g_reverse_scan.load() != 2 || !cp.exch;
   // one (sample, source) pair per thread where it fits in a block of 1024, else 512 threads
-  const int lnth = kLocS * N <= 1024 ? 1024 : kLocThreads;
-  const int lppt = cdiv(kLocS * N, lnth);
+  const int S = cp.S;
+  const int lnth = S * N <= 1024 ? 1024 : kLocThreads;
+  const int lppt = cdiv(S * N, lnth);
   auto kern = k_bwd_chunk<kH64Taps>;
   // taps per source: the integer lags inside one triangle, at most 2*ceil(s_max) + 1
   const bool tap4 = 2 * (int)ceilf(ly->s_max) + 1 <= 4;
-  auto lkern = lnth == 1024 ? (tap4 ? k_bwd_chunk_local<4, 1, 1024> : k_bwd_chunk_local<kH64Taps, 1, 1024>)
-                            : (lppt <= 2 ? k_bwd_chunk_local<kH64Taps, 2, kLocThreads>
-                                         : k_bwd_chunk_local<kH64Taps, 4, kLocThreads>);
+  auto lkern = S == 1 ? (lnth == 1024 ? (tap4 ? k_bwd_chunk_local<4, 1, 1024, 1> : k_bwd_chunk_local<kH64Taps, 1, 1024, 1>)
+                                       : k_bwd_chunk_local<kH64Taps, 2, kLocThreads, 1>)
+                      : (lnth == 1024 ? (tap4 ? k_bwd_chunk_local<4, 1, 1024, 2> : k_bwd_chunk_local<kH64Taps, 1, 1024, 2>)
+                                      : (lppt <= 2 ? k_bwd_chunk_local<kH64Taps, 2, kLocThreads, 2>
+                                                   : k_bwd_chunk_local<kH64Taps, 4, kLocThreads, 2>));
   int rc = DELREC_OK;
   if (local) {
     if (lppt > 4 || lplan.fixed + 512 > lsmem) return DELREC_ERR_UNSUPPORTED;
     rc = set_smem(lkern, lsmem);
     if (rc) return rc;
-    k_short_entries<<<N, 64, 0, st>>>(N, h64.K, h64.CAP, base.boff_stride, base.ent, base.boff, base.tap_l0, sh_idx,
+    k_short_entries<<<N, 64, 0, st>>>(N, ly->K, base.CAP, base.boff_stride, base.ent, base.boff, base.tap_l0, sh_idx,
                                       sh_w);
     DR_LAUNCHED();
-    k_short_pairs<<<1, kLocThreads, 0, st>>>(N, h64.K, h64.CAP, base.boff_stride, base.boff, base.tap_l0, sh_idx, sh_w,
+    k_short_pairs<<<1, kLocThreads, 0, st>>>(N, ly->K, base.CAP, base.boff_stride, base.boff, base.tap_l0, sh_idx, sh_w,
                                              lecap, c_idx, c_w, pairs, pcnt, pcnt + 8);
     DR_LAUNCHED();
   } else {
@@ -1110,15 +1120,15 @@ static int run_chunked(const delrec_layer* ly, const Hyb64Plan& h64, const Chunk
     if (per_sm < 1 || h64.CS * h64.tiles > per_sm * kSMs) return DELREC_ERR_UNSUPPORTED;
   }
   ChunkArgs a{};
-  a.T = T; a.B = B; a.N = N; a.K = h64.K; a.CS = h64.CS; a.NT = h64.NT; a.TAPS = base.TAPS;
-  a.CAPS = h64.CAPS; a.CAP = h64.CAP; a.boff_stride = base.boff_stride;
+  a.T = T; a.B = B; a.N = N; a.K = ly->K; a.CS = h64.CS; a.NT = h64.NT; a.TAPS = base.TAPS;
+  a.CAPS = h64.CAPS; a.CAP = base.CAP; a.boff_stride = base.boff_stride;
   a.gy = base.gy; a.u = base.u; a.keep = base.keep;
   a.tap_l0 = base.tap_l0; a.tap_nt = base.tap_nt; a.tap_w = base.tap_w; a.ent = base.ent; a.boff = base.boff;
   a.dx = base.dx; a.gr = base.gr; a.gz = gz; a.ga_hi = ga_hi; a.ga_lo = ga_lo; a.Np = Np; a.lam = lam;
   a.lif = base.lif; a.grx = base.grx; a.arrive = base.arrive; a.spin_limit = base.spin_limit;
   GzArgs g{};
   g.T = T; g.B = B; g.N = N; g.gz = gz; g.spin_ns = 2000000000ll;
-  DR_CUDA(cudaMemsetAsync(a.arrive, 0, sizeof(unsigned int) * h64.tiles, st));
+  if (!local) DR_CUDA(cudaMemsetAsync(a.arrive, 0, sizeof(unsigned int) * h64.tiles, st));
   scan_mark(0, st);
   for (int ch = cp.nchunks - 1; ch >= 0; --ch) {
     a.t0 = ch * kChunk;
@@ -1127,7 +1137,7 @@ static int run_chunked(const delrec_layer* ly, const Hyb64Plan& h64, const Chunk
     scan_mark(0, st, 1);
     if (local) {
       LocArgs la{a, sh_idx, sh_w, c_idx, c_w, pairs, pcnt, pcnt + 8, lecap};
-      lkern<<<cdiv(B, kLocS), lnth, lsmem, st>>>(la);
+      lkern<<<cdiv(B, S), lnth, lsmem, st>>>(la);
       DR_CUDA(cudaGetLastError());
     } else {
       ChunkArgs ac = a;
@@ -1327,11 +1337,11 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
     h.dx = g->dx; h.gr = gr; h.gz = nullptr; h.lif = a.lif;
     h.grx = grx; h.arrive = arrive; h.spin_limit = 1ll << 22;
     rc = launch_hyb64_t<kSynKmax>(h, s64, st);
-  } else if (h64.ok) {
+  } else if (h64.ok || (kind == DELREC_HYBRID && plan_chunk(ly, bp, h64).ok && g_reverse_scan.load() != 1)) {
     const ChunkPlan cp = plan_chunk(ly, bp, h64);
     Hyb64Args h{};
-    h.T = T; h.B = B; h.N = N; h.K = h64.K; h.CS = h64.CS; h.NT = h64.NT; h.TAPS = bp.TAPS; h.CAPS = h64.CAPS;
-    h.CAP = h64.CAP; h.boff_stride = h64.K + 2;
+    h.T = T; h.B = B; h.N = N; h.K = ly->K; h.CS = h64.CS; h.NT = h64.NT; h.TAPS = bp.TAPS; h.CAPS = h64.CAPS;
+    h.CAP = bp.CAP; h.boff_stride = ly->K + 2;
     h.gy = gy; h.u = u; h.keep = ly->has_keep ? keep : nullptr;
     h.tap_l0 = tl0; h.tap_nt = tnt; h.tap_w = tw; h.ent = ent; h.boff = boff;
     h.dx = g->dx; h.gr = gr; h.gz = gz; h.lif = a.lif;

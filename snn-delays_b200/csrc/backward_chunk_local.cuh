@@ -1,5 +1,5 @@
 // Sample-local form of the chunked reverse scan's step part (see backward_chunk.cuh for
-// the chunking): a block owns kLocS samples and every source neuron of the layer, so the
+// the chunking): a block owns S samples (1 or 2) and every source neuron of the layer, so the
 // step needs no exchange of gr between blocks and no grid-wide wait.  This is possible
 // because, with the long-lag synapses contracted by the chunk GEMM, a step only sums the
 // short-lag synapses (l0_o + k_io <= 7, 12 % at BASELINE config 4): their bucket lists
@@ -20,7 +20,7 @@
 
 namespace delrec {
 
-constexpr int kLocS = 2, kLocThreads = 512, kLocGroup = 8;   // lanes per (source, bucket) pair
+constexpr int kLocSMax = 2, kLocThreads = 512, kLocGroup = 8;   // lanes per (source, bucket) pair
 constexpr int kLocPairCache = 1024;   // pairs staged in shared memory (the rest read from global)
 
 // The short prefix of every source's bucket list (buckets k <= min(K, 7 - l0)) split into
@@ -45,11 +45,11 @@ __global__ void k_short_entries(int N, int K, int CAP, int boff_stride, const in
 struct LocSmem {
   size_t taps, ring, grs, cnt, pairs, fixed;
 };
-__host__ __device__ inline LocSmem loc_smem_plan(int N, int TAPS) {
+__host__ __device__ inline LocSmem loc_smem_plan(int N, int TAPS, int S) {
   LocSmem p;
   p.taps = align256((size_t)N * (2 + TAPS) * 4);                // l0, n, weights
-  p.ring = align256((size_t)N * kChunk * kLocS * 4);            // [N][8][S]
-  p.grs = align256((size_t)kLocS * N * 4);                      // gr(t) [S][N]
+  p.ring = align256((size_t)N * kChunk * S * 4);                // [N][8][S]
+  p.grs = align256((size_t)S * N * 4);                          // gr(t) [S][N]
   p.cnt = 256;                                                  // pairs with lag <= q
   p.pairs = (size_t)kLocPairCache * 16;                        // the first (source, bucket) pairs
   p.fixed = p.taps + p.ring + p.grs + p.cnt + p.pairs;
@@ -207,11 +207,11 @@ struct LocArgs {
   int ecap;                // entries the block's shared-memory cache holds
 };
 
-template <int TPF, int PPT, int NTH>
+template <int TPF, int PPT, int NTH, int S>
 __global__ void __launch_bounds__(NTH, 1) k_bwd_chunk_local(LocArgs la) {
   extern __shared__ __align__(16) unsigned char smem[];
   const ChunkArgs& a = la.c;
-  constexpr int S = kLocS, RING = kChunk, G = kLocGroup;
+  constexpr int RING = kChunk, G = kLocGroup;
   const int N = a.N, T = a.T, B = a.B, TAPS = a.TAPS, tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
   const int b0 = (int)blockIdx.x * S;
@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(NTH, 1) k_bwd_chunk_local(LocArgs la) {
   const size_t BN = (size_t)B * N;
   const int t0 = a.t0, t_hi = a.t_hi;
 
-  const LocSmem P = loc_smem_plan(N, TAPS);
+  const LocSmem P = loc_smem_plan(N, TAPS, S);
   int* tl0 = (int*)smem;                                   // [N]
   int* tnt = tl0 + N;                                      // [N]
   float* tw = (float*)(tnt + N);                           // [N][TAPS]

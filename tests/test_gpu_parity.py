@@ -93,6 +93,10 @@ SHAPES = [
     # per-source widths, a ragged neuron slice and short base lags
     ("hybrid", 7, 64, 256, 1.5, False, True, True, 12.0, 6),
     ("hybrid", 33, 96, 300, 0.7, True, False, False, 6.0, 3),
+    # chunked scan with one sample per step block: small batches (B <= 32) and layers wider
+    # than the 64-sample tiling holds
+    ("hybrid", 26, 20, 300, 0.0, False, True, True, 10.0, 5),
+    ("hybrid", 20, 24, 768, 0.0, False, False, False, 12.0, 8),
 ]
 
 
