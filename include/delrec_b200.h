@@ -122,6 +122,29 @@ int delrec_axonal_backward(const delrec_layer* layer, const delrec_lif* lif,
                            const float* keep, const delrec_grads* grads,
                            void* workspace, size_t workspace_bytes, void* stream);
 
+/* Hard-tap forms of the axonal layer: AxonalRecdelTriton with ste_mode 1 / 2 or approx
+ * (triton_kernels/recdel_base.py:350-445, recdel_bwd_kernel APPROX branch :215-278).
+ * Their forwards are delrec_axonal_forward at half-width s = 1 with the hard taps written
+ * as a delay: the single tap at lag l (lag = clamp(round(d) + 1, 1, .)) is d = l - 1 and
+ * the two-tap interpolation (1 - f) at l, f at l + 1 (l = floor(1 + d)) is d = l - 1 + f,
+ * i.e. max(d, 0).  Backwards:
+ *   DELREC_HARD_STE     the soft triangle's backward over (d, s) -- gfut, dx, dd, ds,
+ *                       dbias -- except dW, which correlates gr with the hard forward's z
+ *                       (taps of d_hard at half-width 1);
+ *   DELREC_HARD_APPROX  the backward of the single-tap forward: d = the hard delays
+ *                       (l - 1), s all 1 and the layer's L sized for them; dd is the
+ *                       straight-through sum_{t,b} gz[t,b,n] (y[t-l-1,b,n] - y[t-l,b,n]);
+ *                       grads->ds must be NULL, d_hard is not read. */
+#define DELREC_HARD_STE 1
+#define DELREC_HARD_APPROX 2
+size_t delrec_axonal_backward_hard_workspace(const delrec_layer* layer);
+int delrec_axonal_backward_hard(const delrec_layer* layer, const delrec_lif* lif, int mode,
+                                const float* gy, const float* u, const float* y,
+                                const float* W, const float* d, const float* s,
+                                const float* d_hard, const float* keep,
+                                const delrec_grads* grads, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
 /* ---- the library's own tensor-core GEMM (tcgen05, bf16 pieces, fp32 accumulate) ------
  * No reference counterpart as an interface: it is the contraction engine behind the
  * weight gradients, the lag-correlation stack and the projections (which the reference

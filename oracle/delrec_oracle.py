@@ -211,6 +211,67 @@ def axonal_scan(x, W, d, lif: OracleLIF, sigma=0.0, p_spread=None, use_sig_p=Fal
     return (y, torch.stack(us)) if record_u else y
 
 
+def hard_lags(d, L, interp=False):
+    """The reference's hard taps (triton_kernels/delays.py:33-47): lag = clamp(round(d)+1,
+    1, L-1), or for the interpolation lag = clamp(floor(1+d), 1, L-1) with the fraction
+    f = clamp(1+d-lag, 0, 1) weighing lag+1 (and 1-f lag).  Returns (lag long, f)."""
+    hi = max(1, L - 1)
+    if interp:
+        pos = 1.0 + d
+        lag = torch.floor(pos).long().clamp(1, hi)
+        return lag, (pos - lag.to(d.dtype)).clamp(0.0, 1.0)
+    return (torch.round(d).long() + 1).clamp(1, hi), torch.zeros_like(d)
+
+
+def axonal_scan_hard(x, W, d, lif: OracleLIF, mode, sigma=0.0, p_spread=None, use_sig_p=False,
+                     bias=None, keep=None, record_u=False):
+    """The axonal layer's hard-tap variants (triton_kernels/recdel_base.py:350-445), their
+    gradients expressed through autograd:
+
+    * mode 1 / 2 ('triton_ste', rounded / interpolated): the forward reads the hard taps
+      z_hard; autograd sees z = z_soft + (z_hard - z_soft).detach(), so the recurrence and
+      the delay / spread gradients are the soft triangle's while the weight gradient
+      correlates with z_hard (recdel_base.py:360-372, 401-412);
+    * mode 3 ('triton_approx'): z = y[t-lag] + (d - d.detach()) (y[t-lag-1] - y[t-lag]).detach()
+      with lag sized on Lmax = round(max d) + 2: the single tap's own backward plus the
+      straight-through delay gradient sum gz (y[t-lag-1] - y[t-lag]) and no spread
+      gradient (recdel_base.py:373-378, 265-278, 416-419)."""
+    T, B, N = x.shape
+    d = d.to(x.dtype)
+    s, s_max = spread(sigma, p_spread, use_sig_p, x.dtype, x.device)
+    L = ring_length(d, s_max)
+    if mode == 3:
+        lag, frac = hard_lags(d.detach(), int(torch.round(d.detach()).max().item()) + 2)
+    else:
+        lag, frac = hard_lags(d.detach(), L, interp=(mode == 2))
+    R = max(L, int(lag.max().item()) + 2)
+    h = triangle(d, s[:, None] if use_sig_p else s, R) if mode != 3 else None
+    hist = x.new_zeros(R, B, N)                  # hist[l] = y[t - l]
+    idx0 = lag.view(1, N, 1).expand(B, N, 1)
+    ys, us = [], []
+    for t in range(T):
+        hp = hist.permute(1, 2, 0)               # (B, N, R)
+        y0 = torch.gather(hp, 2, idx0).squeeze(-1)
+        y1 = torch.gather(hp, 2, idx0 + 1).squeeze(-1)
+        if mode == 3:
+            z = y0 + (d - d.detach()) * (y1 - y0).detach()
+        else:
+            z_hard = (1.0 - frac) * y0 + frac * y1 if mode == 2 else y0
+            z_soft = (hp[..., 1:] * h[:, 1:]).sum(-1)
+            z = z_soft + (z_hard - z_soft).detach()
+        rec = z @ W.t()
+        if bias is not None:
+            rec = rec + bias
+        if keep is not None:
+            rec = rec * keep
+        y = lif.single_step_forward(x[t] + rec)
+        hist = torch.cat([hist[:1], y[None], hist[1:-1]], 0)
+        ys.append(y)
+        us.append(lif.u)
+    y = torch.stack(ys)
+    return (y, torch.stack(us)) if record_u else y
+
+
 def synaptic_scan(x, W, d, lif: OracleLIF, sigma=0.0, p_spread=None, use_sig_p=False,
                   bias=None, keep=None, round_delays=False, record_u=False):
     """Synaptic delay layer.  d (N,N) with d[i,o] target i, source o; the half-width is

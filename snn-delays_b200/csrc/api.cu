@@ -652,6 +652,9 @@ static int cublas_for_device(cublasHandle_t* out) {
 static int cublas_on(cublasHandle_t* h, void* cws, cudaStream_t st);
 
 static inline int pad8(int n) { return (n + 7) / 8 * 8; }
+// k_split_bf16_rows launch: a block per row (grid-stride), a thread per 4 columns
+static inline int split_rows_block(int N) { return std::min(256, std::max(32, (cdiv(pad8(N), 4) + 31) / 32 * 32)); }
+static inline int split_rows_grid(size_t rows) { return (int)std::max<size_t>(1, std::min<size_t>(rows, (size_t)kSMs * 16)); }
 // Split of the dW-type reductions (over the T*B rows) and its tile width.
 static int dw_bn(const delrec_layer* ly) { return gemm_pick_bn(ly->N); }
 static int dw_ksplit(const delrec_layer* ly, int nprod, int nslices) {
@@ -711,7 +714,7 @@ static int dense_dw(const delrec_layer* ly, const float* gr, int nz, int nk, con
                     const DenseBufs& d, cudaStream_t st) {
   const int N = ly->N, T = ly->T, B = ly->B;
   const size_t TBN = (size_t)T * B * pad8(N);
-  k_split_bf16_rows<<<grid_for(TBN, 256), 256, 0, st>>>(gr, (size_t)T * B, N, pad8(N), d.g16, d.g16 + TBN);
+  k_split_bf16_rows<<<split_rows_grid((size_t)T * B), split_rows_block(N), 0, st>>>(gr, (size_t)T * B, N, pad8(N), d.g16, d.g16 + TBN);
   DR_LAUNCHED();
   const GemmSide A = rows_operand(d.g16, d.g16 + TBN, 2, ly);
   const int BN = dw_bn(ly);
@@ -744,9 +747,9 @@ static int dense_dw(const delrec_layer* ly, const float* gr, int nz, int nk, con
 static int syn_cstack(const delrec_layer* ly, const float* gr, const float* y, const DenseBufs& d, cudaStream_t st) {
   const int N = ly->N, T = ly->T, B = ly->B, nk = ly->L;
   const size_t TBN = (size_t)T * B * pad8(N), nn = (size_t)N * N;
-  k_split_bf16_rows<<<grid_for(TBN, 256), 256, 0, st>>>(gr, (size_t)T * B, N, pad8(N), d.g16, d.g16 + TBN);
+  k_split_bf16_rows<<<split_rows_grid((size_t)T * B), split_rows_block(N), 0, st>>>(gr, (size_t)T * B, N, pad8(N), d.g16, d.g16 + TBN);
   DR_LAUNCHED();
-  k_split_bf16_rows<<<grid_for(TBN, 256), 256, 0, st>>>(y, (size_t)T * B, N, pad8(N), d.z16, d.z16 + TBN);
+  k_split_bf16_rows<<<split_rows_grid((size_t)T * B), split_rows_block(N), 0, st>>>(y, (size_t)T * B, N, pad8(N), d.z16, d.z16 + TBN);
   DR_LAUNCHED();
   const GemmSide A = rows_operand(d.g16, d.g16 + TBN, 2, ly);
   const GemmSide Y = rows_operand(d.z16, nullptr, 1, ly);
@@ -1157,7 +1160,16 @@ static int run_chunked(const delrec_layer* ly, const Hyb64Plan& h64, const Chunk
   return DELREC_OK;
 }
 
-static size_t backward_ws(const delrec_layer* ly, int kind) {
+// Hard-tap forms of the axonal backward (AxonalRecdelTriton with ste_mode / approx,
+// recdel_base.py:350-445).  dw_d: the weight gradient correlates gr with the z of the
+// triangle (dw_d, half-width 1) -- the hard forward's taps -- instead of the soft one;
+// st_dd: dd straight-through from the single tap at l = 1 + d.
+struct HardBwd {
+  const float* dw_d;
+  int st_dd;
+};
+
+static size_t backward_ws(const delrec_layer* ly, int kind, bool hard = false) {
   const BwdPlan bp = plan_backward(ly, kind);
   const SrcPlan sp = plan_src(ly);
   const size_t N = ly->N, TBN = (size_t)ly->T * ly->B * N;
@@ -1211,20 +1223,26 @@ static size_t backward_ws(const delrec_layer* ly, int kind) {
   }
   if (kind == DELREC_SYNAPTIC) c.take<float>(N * N);   // ds per pair, summed
   c.take<float>((size_t)sp.splits * N * (bp.TAPS + 1)); // source partials
+  if (hard) {                                          // the hard taps and their pass
+    c.take<int>(N); c.take<int>(N); c.take<float>(N * bp.TAPS); c.take<float>(N);
+    c.take<float>((size_t)sp.splits * N * (bp.TAPS + 1));
+  }
   return c.off;
 }
 
 static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif, const float* gy,
                         const float* u, const float* y, const float* W, const float* d,
                         const float* offsets, const float* s, const float* keep,
-                        const delrec_grads* g, void* ws, size_t wsb, cudaStream_t st) {
+                        const delrec_grads* g, void* ws, size_t wsb, cudaStream_t st,
+                        const HardBwd* hb = nullptr) {
   int rc = check_layer(ly, kind);
   if (rc) return rc;
   if (!lif || !gy || !u || !y || !W || !d || !s || !g || !g->dx) return DELREC_ERR_ARG;
   if (kind == DELREC_HYBRID && !offsets) return DELREC_ERR_ARG;
   if (ly->has_keep && !keep) return DELREC_ERR_ARG;
   if (((uintptr_t)ws & 255) != 0) return DELREC_ERR_WORKSPACE;
-  if (wsb < backward_ws(ly, kind)) return DELREC_ERR_WORKSPACE;
+  if (hb && (kind != DELREC_AXONAL || (hb->st_dd && g->ds))) return DELREC_ERR_ARG;
+  if (wsb < backward_ws(ly, kind, hb != nullptr)) return DELREC_ERR_WORKSPACE;
   const BwdPlan bp = plan_backward(ly, kind);
   if (!bp.ok || bp.MM > kMMMax) return DELREC_ERR_UNSUPPORTED;
   // k_source_pass keeps each neuron's spike history in 128 bits
@@ -1392,17 +1410,39 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
       if (pad8(N) != N)
         DR_CUDA(cudaMemsetAsync(dbf.z16, 0, (size_t)T * B * pad8(N) * 2 * nz * sizeof(__nv_bfloat16), st));
     }
-    if (g->dW || need_src) {
-      const int wz = g->dW ? 1 : 0, warm = ly->L - 1 + bp.MM;
+    const int warm = ly->L - 1 + bp.MM;
+    auto src_pass = [&](const SrcArgs& a_, int wz) {
       if (bp.MM == 0) {
-        if (bp.TAPS <= 4) k_source_pass<4, 0><<<sgrid, 256, 0, st>>>(sa, wz, warm, dbf.z16);
-        else if (bp.TAPS <= 8) k_source_pass<8, 0><<<sgrid, 256, 0, st>>>(sa, wz, warm, dbf.z16);
-        else k_source_pass<16, 0><<<sgrid, 256, 0, st>>>(sa, wz, warm, dbf.z16);
+        if (bp.TAPS <= 4) k_source_pass<4, 0><<<sgrid, 256, 0, st>>>(a_, wz, warm, dbf.z16);
+        else if (bp.TAPS <= 8) k_source_pass<8, 0><<<sgrid, 256, 0, st>>>(a_, wz, warm, dbf.z16);
+        else k_source_pass<16, 0><<<sgrid, 256, 0, st>>>(a_, wz, warm, dbf.z16);
       } else {
-        if (bp.TAPS <= 4) k_source_pass<4, 3><<<sgrid, 256, 0, st>>>(sa, wz, warm, dbf.z16);
-        else if (bp.TAPS <= 8) k_source_pass<8, 3><<<sgrid, 256, 0, st>>>(sa, wz, warm, dbf.z16);
-        else k_source_pass<16, 3><<<sgrid, 256, 0, st>>>(sa, wz, warm, dbf.z16);
+        if (bp.TAPS <= 4) k_source_pass<4, 3><<<sgrid, 256, 0, st>>>(a_, wz, warm, dbf.z16);
+        else if (bp.TAPS <= 8) k_source_pass<8, 3><<<sgrid, 256, 0, st>>>(a_, wz, warm, dbf.z16);
+        else k_source_pass<16, 3><<<sgrid, 256, 0, st>>>(a_, wz, warm, dbf.z16);
       }
+    };
+    // hard-tap weight gradient: the soft pass gives the sums, a second pass over the
+    // hard taps writes the z pieces (its partial sums are not used)
+    const bool hard_dw = hb && hb->dw_d && g->dW;
+    if (need_src || (g->dW && !hard_dw)) {
+      src_pass(sa, g->dW && !hard_dw ? 1 : 0);
+      DR_LAUNCHED();
+    }
+    if (hard_dw) {
+      int* hl0 = c.take<int>(N);
+      int* hnt = c.take<int>(N);
+      float* hw = c.take<float>((size_t)N * bp.TAPS);
+      float* ones = c.take<float>(N);
+      float* hpart = c.take<float>((size_t)sp.splits * N * (bp.TAPS + 1));
+      if (!c.ok) return DELREC_ERR_WORKSPACE;
+      k_fill_f32<<<cdiv(N, 256), 256, 0, st>>>(ones, N, 1.f);
+      DR_LAUNCHED();
+      k_taps<<<cdiv(N, 256), 256, 0, st>>>(hb->dw_d, ones, N, ly->L - 1, bp.TAPS, 1, hl0, hnt, hw);
+      DR_LAUNCHED();
+      SrcArgs sh = sa;
+      sh.tap_l0 = hl0; sh.tap_nt = hnt; sh.tap_w = hw; sh.part = hpart;
+      src_pass(sh, 1);
       DR_LAUNCHED();
     }
     if (g->dW) {
@@ -1447,7 +1487,7 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
     const bool src_dd = kind != DELREC_SYNAPTIC;
     k_source_finalize<<<cdiv(N, 128), 128, 0, st>>>(N, bp.TAPS, sp.splits, spart, d, s, tl0, tnt,
                                                      g->dbias, src_dd ? g->dd : nullptr,
-                                                     src_dd ? g->ds : nullptr);
+                                                     src_dd ? g->ds : nullptr, hb ? hb->st_dd : 0);
     DR_LAUNCHED();
   }
   return DELREC_OK;
@@ -1580,6 +1620,25 @@ int delrec_axonal_backward(const delrec_layer* ly, const delrec_lif* lif, const 
                            const float* y, const float* W, const float* d, const float* s, const float* keep,
                            const delrec_grads* g, void* ws, size_t wsb, void* stream) {
   return run_backward(ly, DELREC_AXONAL, lif, gy, u, y, W, d, nullptr, s, keep, g, ws, wsb, (cudaStream_t)stream);
+}
+size_t delrec_axonal_backward_hard_workspace(const delrec_layer* ly) {
+  return ly ? backward_ws(ly, DELREC_AXONAL, true) : 0;
+}
+int delrec_axonal_backward_hard(const delrec_layer* ly, const delrec_lif* lif, int mode, const float* gy,
+                                const float* u, const float* y, const float* W, const float* d,
+                                const float* s, const float* d_hard, const float* keep,
+                                const delrec_grads* g, void* ws, size_t wsb, void* stream) {
+  HardBwd hb{};
+  if (mode == DELREC_HARD_STE) {
+    if (!d_hard) return DELREC_ERR_ARG;
+    hb.dw_d = d_hard;
+  } else if (mode == DELREC_HARD_APPROX) {
+    hb.st_dd = 1;
+  } else {
+    return DELREC_ERR_ARG;
+  }
+  return run_backward(ly, DELREC_AXONAL, lif, gy, u, y, W, d, nullptr, s, keep, g, ws, wsb,
+                      (cudaStream_t)stream, &hb);
 }
 int delrec_synaptic_backward(const delrec_layer* ly, const delrec_lif* lif, const float* gy, const float* u,
                              const float* y, const float* W, const float* d, const float* s, const float* keep,

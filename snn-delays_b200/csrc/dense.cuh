@@ -28,16 +28,39 @@ __global__ void k_split_bf16(const float* __restrict__ x, size_t n, __nv_bfloat1
 
 // hi + lo bf16 pieces of a (rows, N) fp32 matrix written with row stride Np >= N (the
 // GEMM operand layout; columns N..Np-1 are zero)
+// (blocks stride over rows, threads over groups of 4 columns: no per-element 64-bit
+// index division; 16-byte loads and 8-byte stores when N is a multiple of 4)
 __global__ void k_split_bf16_rows(const float* __restrict__ x, size_t rows, int N, int Np,
                                   __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
-  const size_t total = rows * (size_t)Np;
-  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
-    const size_t r = e / Np;
-    const int n = (int)(e % Np);
-    const float v = n < N ? x[r * N + n] : 0.f;
-    const __nv_bfloat16 h = __float2bfloat16_rn(v);
-    hi[e] = h;
-    lo[e] = __float2bfloat16_rn(v - __bfloat162float(h));
+  const bool vec = (N & 3) == 0 && (((uintptr_t)x) & 15) == 0;
+  for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float* xr = x + r * N;
+    __nv_bfloat16* hr = hi + r * Np;
+    __nv_bfloat16* lr = lo + r * Np;
+    for (int c = threadIdx.x * 4; c < Np; c += blockDim.x * 4) {
+      float v[4];
+      if (vec && c + 4 <= N) {
+        const float4 f = __ldcs((const float4*)(xr + c));
+        v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v[q] = c + q < N ? xr[c + q] : 0.f;
+      }
+      __nv_bfloat16 h[4], l[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        h[q] = __float2bfloat16_rn(v[q]);
+        l[q] = __float2bfloat16_rn(v[q] - __bfloat162float(h[q]));
+      }
+      if (c + 4 <= Np) {   // Np is a multiple of 8: 8-byte aligned groups
+        *(uint2*)(hr + c) = *(const uint2*)h;
+        *(uint2*)(lr + c) = *(const uint2*)l;
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (c + q < Np) { hr[c + q] = h[q]; lr[c + q] = l[q]; }
+      }
+    }
   }
 }
 

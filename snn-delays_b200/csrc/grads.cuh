@@ -302,10 +302,12 @@ __global__ void __launch_bounds__(256, 2) k_source_pass(SrcArgs a, int want_z, i
 }
 
 // Combine the row splits: db[n], and dd[n], ds[n] from dmask via the triangle derivatives.
+// st_dd != 0 (single-tap forward at the integer lag l = 1 + d, recdel_base.py:265-278):
+// dd[n] = dmask[l + 1] - dmask[l] straight-through instead, ds untouched.
 __global__ void k_source_finalize(int N, int TAPS, int splits, const float* __restrict__ part,
                                   const float* __restrict__ d, const float* __restrict__ s,
                                   const int* __restrict__ l0, const int* __restrict__ nt,
-                                  float* db, float* dd, float* ds) {
+                                  float* db, float* dd, float* ds, int st_dd) {
   const int n = blockIdx.x * blockDim.x + threadIdx.x;
   if (n >= N) return;
   float gsum = 0.f;
@@ -314,6 +316,17 @@ __global__ void k_source_finalize(int N, int TAPS, int splits, const float* __re
   if (!dd && !ds) return;
   const Tri tr = make_tri(d[n], s[n]);
   const int lo = l0[n], cnt = nt[n];
+  if (st_dd) {
+    const int j0 = (int)floorf(tr.onepd + 0.5f) - lo;
+    float m0 = 0.f, m1 = 0.f;
+    for (int sp = 0; sp < splits; ++sp) {
+      const float* pr = part + ((size_t)sp * N + n) * (TAPS + 1);
+      if (j0 >= 0 && j0 < cnt) m0 += pr[j0];
+      if (j0 + 1 >= 0 && j0 + 1 < cnt) m1 += pr[j0 + 1];
+    }
+    if (dd) dd[n] = m1 - m0;
+    return;
+  }
   float gd = 0.f, gs = 0.f;
   for (int j = 0; j < cnt; ++j) {
     float m = 0.f;

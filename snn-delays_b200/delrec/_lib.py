@@ -20,6 +20,7 @@ OK = 0
 ERRORS = {1: "invalid argument", 2: "CUDA error", 3: "workspace too small or misaligned",
           4: "unsupported shape"}
 AXONAL, SYNAPTIC, HYBRID = 0, 1, 2
+HARD_STE, HARD_APPROX = 1, 2     # delrec_axonal_backward_hard modes
 SURR_TRIANGLE, SURR_ATAN = 0, 1
 
 
@@ -59,6 +60,8 @@ _SIGS = {
     "delrec_synaptic_forward": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _S, _P]),
     "delrec_hybrid_forward": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _S, _P]),
     "delrec_axonal_backward": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _S, _P]),
+    "delrec_axonal_backward_hard_workspace": (_S, [_P]),
+    "delrec_axonal_backward_hard": (_I, [_P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _S, _P]),
     "delrec_synaptic_backward": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _S, _P]),
     "delrec_hybrid_backward": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _S, _P]),
     "delrec_hybrid_delay_grad": (_I, [_I, _I, _P, _P, _P, _F, _P, _P]),

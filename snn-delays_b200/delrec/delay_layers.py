@@ -23,7 +23,8 @@ from .neuron import Dropout, LIFNode, MemoryModule
 
 # forward_version values that select the CUDA kernels; the pure-PyTorch reference scans
 # ('v1', 'v2') are not shipped with this package.
-_CUDA_VERSIONS = (None, "triton_exact", "eventdriven", "hybrid_triton", "cuda")
+_CUDA_VERSIONS = (None, "triton_exact", "triton_approx", "triton_ste", "eventdriven", "hybrid_triton",
+                  "cuda")
 AXONAL_CUDA_DEFAULT = "triton_exact"
 SYNAPTIC_CUDA_DEFAULT = "eventdriven"
 
@@ -42,12 +43,23 @@ def _check_cuda(x_seq, layer):
         raise NotImplementedError(
             f"forward_version={fv!r} is the reference's pure-PyTorch scan, which this package "
             "does not ship; leave forward_version unset to run the CUDA kernels")
-    if fv in ("triton_approx", "triton_ste"):
-        raise NotImplementedError(f"forward_version={fv!r} is not provided; use round_delays")
     if fv not in _CUDA_VERSIONS:
         raise ValueError(f"unknown forward_version {fv!r}")
     if getattr(layer.neuron_module, "decay_input", False):
         raise NotImplementedError("decay_input=True is not supported by the CUDA kernels")
+
+
+def _axonal_variant(layer):
+    """forward_version -> the axonal scan's (approx, ste_mode) (delay_layers.py:204-211,
+    delay_layers_triton.py:60-61): 'triton_approx' is the straight-through single-tap
+    scan, 'triton_ste' the hard-tap forward with the soft backward -- rounded taps, or
+    the 2-tap interpolation when config.ste_round_forward is False."""
+    fv = getattr(layer, "forward_version", None)
+    if fv == "triton_approx":
+        return dict(approx=True, ste_mode=0)
+    if fv == "triton_ste":
+        return dict(approx=False, ste_mode=1 if getattr(layer.config, "ste_round_forward", True) else 2)
+    return dict(approx=False, ste_mode=0)
 
 
 def _keep_mask(layer, B, N, x_seq):
@@ -195,7 +207,7 @@ class axonal_recdel(MemoryModule):
         if self.step_mode == "s":
             raise NotImplementedError("single-step mode is not supported")
         _check_cuda(x_seq, self)
-        return self.multi_step_forward_triton(x_seq)
+        return self.multi_step_forward_triton(x_seq, **_axonal_variant(self))
 
 
 class synaptic_recdel(axonal_recdel):
@@ -290,4 +302,4 @@ class common_recdel(axonal_recdel):
         if self.step_mode == "s":
             raise NotImplementedError("single-step mode is not supported")
         _check_cuda(x_seq, self)
-        return self.multi_step_forward_triton(x_seq)
+        return self.multi_step_forward_triton(x_seq, **_axonal_variant(self))

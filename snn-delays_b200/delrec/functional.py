@@ -161,7 +161,9 @@ def layer_forward(kind, x, W, bias, d, offsets, s, keep, L, K, lif, s_max=None, 
     return y, u, desc
 
 
-def layer_backward(kind, desc, lif, gy, u, y, W, d, offsets, s, keep, need):
+def layer_backward(kind, desc, lif, gy, u, y, W, d, offsets, s, keep, need, hard=None):
+    """The layer's backward through the C-ABI; ``hard`` = (mode, d_hard) runs the axonal
+    hard-tap backward (delrec_axonal_backward_hard) instead."""
     gy = gy.detach().contiguous()
     _lib.require_cuda(gy)
     T, B, N = gy.shape
@@ -180,10 +182,16 @@ def layer_backward(kind, desc, lif, gy, u, y, W, d, offsets, s, keep, need):
     wsfn = {_lib.AXONAL: "delrec_axonal_backward_workspace",
             _lib.SYNAPTIC: "delrec_synaptic_backward_workspace",
             _lib.HYBRID: "delrec_hybrid_backward_workspace"}[kind]
+    if hard is not None:
+        wsfn = "delrec_axonal_backward_hard_workspace"
     nbytes = getattr(_lib.lib(), wsfn)(ctypes.byref(desc))
     ws = _lib.workspace(nbytes, dev)
     st = _lib.stream_ptr(dev)
-    if kind == _lib.HYBRID:
+    if hard is not None:
+        mode, d_hard = hard
+        _run("delrec_axonal_backward_hard", ctypes.byref(desc), ctypes.byref(lif), mode, P(gy), P(u),
+             P(y), P(W), P(d), P(s), P(d_hard), P(keep), ctypes.byref(g), P(ws), ws.numel(), st)
+    elif kind == _lib.HYBRID:
         _run("delrec_hybrid_backward", ctypes.byref(desc), ctypes.byref(lif), P(gy), P(u), P(y), P(W),
              P(d), P(offsets), P(s), P(keep), ctypes.byref(g), P(ws), ws.numel(), st)
     else:
@@ -204,17 +212,47 @@ def _dp_from_ds(ds, p_spread, sigma):
 # ---------------------------------------------------------------------------------
 
 
+def hard_delays(d, dmax, L, mode):
+    """The hard taps of the rounded / interpolated axonal forwards written as delays of a
+    half-width-1 triangle (delays.py:33-47 build_lag / build_lag_interp, taken on the
+    reference's own ring length L), and the largest of them as a host float.
+    mode 1 (STE rounded) and 3 (approx): one tap at lag = clamp(round(d) + 1, 1, L - 1),
+    delay lag - 1; mode 2 (STE interpolated): lag = clamp(floor(1 + d), 1, L - 1),
+    f = clamp(1 + d - lag, 0, 1), delay (lag - 1) + f, whose triangle weighs lag by 1 - f
+    and lag + 1 by f exactly."""
+    import numpy as np
+    dd = d.detach().float()
+    hi = float(max(1, L - 1))
+    if mode == 2:
+        pos = 1.0 + dd
+        lag = torch.floor(pos).clamp_(1.0, hi)
+        d_hard = (lag - 1.0) + (pos - lag).clamp_(0.0, 1.0)
+        p32 = np.float32(1.0) + np.float32(dmax)
+        l32 = np.float32(min(max(np.floor(p32), 1.0), hi))
+        dh_max = float((l32 - np.float32(1.0)) + np.float32(min(max(p32 - l32, 0.0), 1.0)))
+    else:
+        d_hard = (torch.round(dd) + 1.0).clamp_(1.0, hi) - 1.0
+        dh_max = min(max(float(np.round(np.float32(dmax))) + 1.0, 1.0), hi) - 1.0
+    return d_hard.contiguous(), dh_max
+
+
 class AxonalRecdelTriton(torch.autograd.Function):
     """Axonal delay layer (per-source delay d (N,)).  Same arguments as the reference's
     ``AxonalRecdelTriton.apply`` (recdel_base.py:351-353); ``drop`` may be the (T,B,N)
-    expanded fixed mask or the (B,N) mask itself."""
+    expanded fixed mask or the (B,N) mask itself.
+
+    ``ste_mode`` 1 / 2 (forward_version 'triton_ste'): the forward runs on the hard taps
+    (rounded lag, or the 2-tap interpolation), the backward is the soft triangle's except
+    the weight gradient, which correlates with the forward's hard z (recdel_base.py:
+    356-372, 401-412).  ``approx`` ('triton_approx'): the single rounded tap forward and
+    its own backward, with the straight-through delay gradient
+    dd = sum gz(t) (y(t-lag-1) - y(t-lag)) and no spread gradient (recdel_base.py:373-378,
+    265-278, 416-419).  The hard forwards run the same kernels as the soft one, at
+    half-width 1 with the taps written as delays (``hard_delays``)."""
 
     @staticmethod
     def forward(ctx, x, W, bias, d, p_spread, drop, sigma, tau, v_th, v_reset, use_sig_p,
                 detach_reset, surr_id, gamma=1.0, approx=False, ste_mode=0, alpha=2.0):
-        if approx or ste_mode:
-            raise NotImplementedError("the rounded-lag 'triton_approx' / 'triton_ste' variants are "
-                                      "not provided; use round_delays for an STE-rounded forward")
         T, B, N = x.shape
         s = half_widths(sigma, p_spread, use_sig_p, N, x.device)
         sm = _s_max(sigma, p_spread, use_sig_p, s)
@@ -227,20 +265,48 @@ class AxonalRecdelTriton(torch.autograd.Function):
         lif = _lib.lif_struct(tau, v_th, v_reset, detach_reset, surr_id, gamma, alpha)
         keep = _keep2d(drop, B, N)
         b = bias.detach().float().contiguous() if bias is not None else None
-        y, u, desc = layer_forward(_lib.AXONAL, x, W, b, d, None, s, keep, L, 0, lif, s_max=sm)
-        ctx.save_for_backward(u, y, W, d, s, keep if keep is not None else torch.empty(0), p_spread)
-        ctx.meta = (desc, lif, sigma, use_sig_p, keep is not None)
+        ste_mode = int(ste_mode) if ste_mode else 0
+        if ste_mode not in (0, 1, 2):
+            raise ValueError(f"ste_mode must be 0, 1 or 2, got {ste_mode}")
+        mode = ste_mode if ste_mode else (3 if approx else 0)
+        if mode == 0:
+            y, u, desc = layer_forward(_lib.AXONAL, x, W, b, d, None, s, keep, L, 0, lif, s_max=sm)
+            d_hard = torch.empty(0)
+        else:
+            # approx sizes its taps on Lmax = round(max d) + 2 (recdel_base.py:374-375)
+            Lh = L if mode != 3 else int(round(dmax)) + 2
+            d_hard, dh_max = hard_delays(d, dmax, Lh, 2 if mode == 2 else 1)
+            ones = torch.ones(N, device=x.device, dtype=torch.float32)
+            Lf = ring_length(torch.tensor(dh_max, dtype=torch.float32), torch.tensor(1.0))
+            y, u, desc = layer_forward(_lib.AXONAL, x, W, b, d_hard, None, ones, keep, Lf, 0, lif,
+                                       s_max=1.0)
+            if mode != 3:   # the STE backward runs on the soft triangle's ring
+                desc = _layer(_lib.AXONAL, T, B, N, L, 0, b is not None, keep is not None, sm)
+        ctx.save_for_backward(u, y, W, d, s, keep if keep is not None else torch.empty(0), p_spread,
+                              d_hard)
+        ctx.meta = (desc, lif, sigma, use_sig_p, keep is not None, mode)
         return y
 
     @staticmethod
     def backward(ctx, gy):
-        u, y, W, d, s, keep, p_spread = ctx.saved_tensors
-        desc, lif, sigma, use_sig_p, has_keep = ctx.meta
+        u, y, W, d, s, keep, p_spread, d_hard = ctx.saved_tensors
+        desc, lif, sigma, use_sig_p, has_keep, mode = ctx.meta
         need = dict(W=ctx.needs_input_grad[1], bias=ctx.needs_input_grad[2],
                     d=ctx.needs_input_grad[3], s=use_sig_p and ctx.needs_input_grad[4])
-        dx, dW, db, dd, ds = layer_backward(_lib.AXONAL, desc, lif, gy, u, y, W.detach().contiguous(),
-                                            d.detach().contiguous(), None, s,
-                                            keep if has_keep else None, need)
+        Wc = W.detach().contiguous()
+        kp = keep if has_keep else None
+        if mode == 0:
+            dx, dW, db, dd, ds = layer_backward(_lib.AXONAL, desc, lif, gy, u, y, Wc,
+                                                d.detach().contiguous(), None, s, kp, need)
+        elif mode == 3:
+            need["s"] = False
+            ones = torch.ones_like(d_hard)
+            dx, dW, db, dd, ds = layer_backward(_lib.AXONAL, desc, lif, gy, u, y, Wc, d_hard, None,
+                                                ones, kp, need, hard=(_lib.HARD_APPROX, None))
+        else:
+            dx, dW, db, dd, ds = layer_backward(_lib.AXONAL, desc, lif, gy, u, y, Wc,
+                                                d.detach().contiguous(), None, s, kp, need,
+                                                hard=(_lib.HARD_STE, d_hard))
         dp = _dp_from_ds(ds, p_spread, sigma) if ds is not None else None
         return (dx, dW, db, dd, dp) + (None,) * 12
 

@@ -2,7 +2,7 @@
 
 Run here (it needs the read-only reference checkout; the GPU box never runs it):
 
-    python tests/golden/make_golden.py <path of the reference checkout>
+    python tests/golden/make_golden.py <path of the reference checkout> [--hard-only]
 
 For every case it runs, on identical seeded inputs,
   * the reference's canonical pure-PyTorch scans ``multi_step_forward_v2``
@@ -36,6 +36,7 @@ from delrec import delay_layers_pytorch as ref_scans  # noqa: E402
 from delrec.triton_kernels import recdel_base as ref_ax  # noqa: E402
 from delrec.triton_kernels import synaptic_eventdriven as ref_ed  # noqa: E402
 from delrec.triton_kernels import synaptic_hybrid as ref_hy  # noqa: E402
+from delrec.triton_kernels.delays import build_lag, build_lag_interp  # noqa: E402
 from delrec.triton_kernels.delays import build_mask, build_syn_mask  # noqa: E402
 from oracle.delrec_oracle import OracleLIF, ATanSpike, TriangleSpike  # noqa: E402
 
@@ -180,6 +181,68 @@ def run_triton_axonal(inp, sigma, use_sig_p, tau, v_reset, surr, detach_reset):
     return out
 
 
+def run_triton_axonal_hard(inp, sigma, use_sig_p, tau, v_reset, surr, detach_reset, mode):
+    """The hard-tap variants of the reference's axonal scan (mode 1 / 2: ste_mode 1 / 2,
+    mode 3: approx) on the interpreter, following AxonalRecdelTriton.forward / backward
+    (recdel_base.py:350-445) and recdel_triton_backward's host reductions (:288-342)."""
+    x, W, d, p = inp["x"], inp["W"], inp["d"], inp["p"]
+    T, B, N = x.shape
+    decay, charge, vr, soft = _lif_consts(tau, v_reset)
+    frac = torch.zeros(N)
+    if mode in (1, 2):
+        mask, L = build_mask(d, sigma, p, use_sig_p)
+        if mode == 1:
+            lag = build_lag(d, L)
+        else:
+            lag, frac = build_lag_interp(d, L)
+        fwd, approx = mode, False
+    else:
+        Lmax = int(torch.round(d).max().item()) + 2
+        lag = build_lag(d, Lmax)
+        mask, L = torch.zeros(N, 2), 2
+        fwd, approx = 1, True
+    keep = inp["keep"] if inp["keep"] is not None else torch.ones(B, N)
+    drop = keep.unsqueeze(0).expand(T, B, N).contiguous()
+    bias = inp["bias"] if inp["bias"] is not None else torch.zeros(N)
+    Wt = W.t().contiguous()
+    y, u, rec, z = (torch.empty_like(x) for _ in range(4))
+    BN = 1 << (N - 1).bit_length()
+    bk = min(64, BN)
+    ref_ax.recdel_fwd_kernel[(triton_cdiv(B, 16),)](
+        x, drop, Wt, bias, mask, lag, frac, y, u, rec, z, T, B, N,
+        x.stride(0), x.stride(1), x.stride(2), Wt.stride(0), Wt.stride(1),
+        mask.stride(0), mask.stride(1), decay, charge, 1.0, vr,
+        BLOCK_B=16, BLOCK_N=BN, BK=bk, L=L, SOFT=soft, FWD=fwd)
+    gy = inp["gy"]
+    gz, gr, dx = (torch.empty_like(x) for _ in range(3))
+    ddst = torch.zeros(N)
+    sid = 1 if surr == "atan" else 0
+    ref_ax.recdel_bwd_kernel[(triton_cdiv(B, 16),)](
+        gy, u, drop, W, mask, lag, y, gz, gr, dx, ddst, T, B, N,
+        gy.stride(0), gy.stride(1), gy.stride(2), W.stride(0), W.stride(1),
+        mask.stride(0), mask.stride(1), decay, 1.0, vr, 1.0, 2.0,
+        BLOCK_B=16, BLOCK_N=BN, BK=bk, L=L, SOFT=soft, DETACH=bool(detach_reset), SURR=sid,
+        APPROX=approx)
+    dW = gr.reshape(T * B, N).t() @ z.reshape(T * B, N)
+    db = gr.reshape(T * B, N).sum(0)
+    out = dict(y=y, u=u, z=z, gr=gr, dx=dx, dW=dW, dbias=db, lag=lag, frac=frac)
+    if approx:
+        out["dd"] = ddst
+        return out
+    dmask = torch.zeros(N, L)
+    for l in range(1, min(L, T)):
+        dmask[:, l] = (gz[l:T] * y[0:T - l]).sum(dim=(0, 1))
+    d_ = d.clone().requires_grad_(True)
+    p_ = p.clone().requires_grad_(use_sig_p) if use_sig_p else None
+    m2, _ = build_mask(d_, sigma, p_, use_sig_p)
+    targets = [d_] + ([p_] if use_sig_p else [])
+    grads = torch.autograd.grad(m2, targets, grad_outputs=dmask, allow_unused=True)
+    out["dd"] = grads[0]
+    if use_sig_p:
+        out["dp"] = grads[1]
+    return out
+
+
 def run_triton_synaptic(kind, inp, sigma, use_sig_p, tau, v_reset, surr, detach_reset):
     """Reference event-driven scatter + dense BPTT kernels (synaptic_eventdriven.py) on the
     interpreter, with the Cstack reductions of EventDrivenSyn / HybridSynDelay.backward."""
@@ -273,8 +336,38 @@ CASES = [
 ]
 
 
+# hard-tap axonal variants: name, seed, T, B, N, sigma, use_sig_p, bias, dropout, dmax,
+# tau, v_reset, surr, detach, special delays (None: uniform in [0, dmax))
+HARD_CASES = [
+    ("hard_basic", 11, 12, 3, 8, 0.0, False, False, False, 4.0, 2.0, 0.0, "atan", False, None),
+    ("hard_sigp_bias", 12, 14, 4, 12, 1.0, True, True, False, 5.0, 2.0, None, "triangle", False, None),
+    ("hard_odd_drop", 13, 16, 5, 33, 0.5, False, True, True, 6.0, 3.0, 0.0, "atan", True, None),
+    # ties of the rounding (half to even), integer delays and a negative delay
+    ("hard_edges", 14, 15, 3, 10, 0.5, False, False, False, 4.0, 2.0, 0.0, "atan", False,
+     [0.0, 0.5, 1.5, 2.5, 1.0, 3.0, -0.4, 2.25, 3.75, 0.99]),
+]
+
+
+def make_hard():
+    out = []
+    for (name, seed, T, B, N, sigma, sigp, bias, drop, dmax, tau, vr, surr, det, dspec) in HARD_CASES:
+        inp = make_inputs(seed, T, B, N, "axonal", sigma, sigp, bias, drop, dmax)
+        if dspec is not None:
+            inp["d"] = torch.tensor(dspec)
+        for mode in (1, 2, 3):
+            res = run_triton_axonal_hard(inp, sigma, sigp, tau, vr, surr, det, mode)
+            meta = dict(name=name, kind="axonal", mode=mode, T=T, B=B, N=N, sigma=sigma,
+                        use_sig_p=sigp, tau=tau, v_reset=vr, surr=surr, detach_reset=det)
+            out.append(dict(meta=meta, inputs=inp, triton=res))
+            print(f"{name:16s} mode {mode}: spikes {int(res['y'].sum())}", flush=True)
+    torch.save(out, os.path.join(HERE, "ax_hard.pt"))
+
+
 def main():
     torch.set_num_threads(4)
+    if "--hard-only" in sys.argv:
+        make_hard()
+        return
     for (name, kind, seed, T, B, N, sigma, sigp, bias, drop, dmax, K, tau, vr, surr,
          det) in CASES:
         inp = make_inputs(seed, T, B, N, kind, sigma, sigp, bias, drop, dmax, K)
@@ -306,6 +399,7 @@ def main():
         dd_cases.append(dict(sigma=sigma, d=d, W=W, C=C, dd=dd))
     torch.save(dd_cases, os.path.join(HERE, "hybrid_dd_edges.pt"))
     print("hybrid_dd_edges ok")
+    make_hard()
 
 
 if __name__ == "__main__":

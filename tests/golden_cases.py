@@ -13,7 +13,13 @@ GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
 def case_names():
     return sorted(os.path.basename(p)[:-3] for p in glob.glob(os.path.join(GOLDEN, "*.pt"))
-                  if not os.path.basename(p).startswith("hybrid_dd"))
+                  if not os.path.basename(p).startswith(("hybrid_dd", "ax_hard")))
+
+
+def hard_cases():
+    """The axonal hard-tap fixtures: a list of {meta (mode 1/2 = triton_ste rounded /
+    interpolated, 3 = triton_approx), inputs, triton}."""
+    return torch.load(os.path.join(GOLDEN, "ax_hard.pt"), weights_only=False)
 
 
 def load(name):
@@ -28,6 +34,8 @@ def oracle_run(case, dtype=torch.float32, device="cpu"):
     """Forward + BPTT of one golden case through the oracle; returns a dict like the
     fixture's ``v2`` entry (tensors on the CPU).  ``device``/``dtype`` choose where and in
     which precision the oracle's torch code is evaluated."""
+    if case["meta"].get("mode", 0):
+        return oracle_run_hard(case, dtype, device)
     meta, inp = case["meta"], case["inputs"]
     c = lambda t: None if t is None else t.to(device=device, dtype=dtype).clone()
     x = c(inp["x"]).requires_grad_(True)
@@ -53,6 +61,31 @@ def oracle_run(case, dtype=torch.float32, device="cpu"):
     if b is not None:
         out["dbias"] = b.grad
     return {k: v.cpu() for k, v in out.items()}
+
+
+def oracle_run_hard(case, dtype=torch.float32, device="cpu"):
+    """Forward + BPTT of one hard-tap fixture through ``axonal_scan_hard``."""
+    meta, inp = case["meta"], case["inputs"]
+    c = lambda t: None if t is None else t.to(device=device, dtype=dtype).clone()
+    x = c(inp["x"]).requires_grad_(True)
+    W = c(inp["W"]).requires_grad_(True)
+    d = c(inp["d"]).requires_grad_(True)
+    p = c(inp["p"]).requires_grad_(meta["use_sig_p"])
+    b = c(inp["bias"])
+    if b is not None:
+        b.requires_grad_(True)
+    lif = O.OracleLIF(tau=meta["tau"], v_threshold=1.0, v_reset=meta["v_reset"],
+                      surrogate=surrogate(meta), detach_reset=meta["detach_reset"])
+    y, u = O.axonal_scan_hard(x, W, d, lif, meta["mode"], sigma=meta["sigma"], p_spread=p,
+                              use_sig_p=meta["use_sig_p"], bias=b, keep=c(inp["keep"]),
+                              record_u=True)
+    (y * c(inp["gy"])).sum().backward()
+    out = dict(y=y.detach(), u=u.detach(), dx=x.grad, dW=W.grad, dd=d.grad)
+    if meta["use_sig_p"] and p.grad is not None:
+        out["dp"] = p.grad
+    if b is not None:
+        out["dbias"] = b.grad
+    return {k: v.cpu() for k, v in out.items() if v is not None}
 
 
 def subset_case(case, samples):

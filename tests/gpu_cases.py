@@ -48,10 +48,11 @@ def run_cuda(meta, inp):
     layer = layer_ns(meta)
     if meta["kind"] == "axonal":
         sid = 1 if meta["surr"] == "atan" else 0
+        mode = meta.get("mode", 0)   # 1 / 2: triton_ste rounded / interpolated, 3: triton_approx
         y = Fn.AxonalRecdelTriton.apply(x, W, b, base, p if meta["use_sig_p"] else None, keep,
                                         meta["sigma"], meta["tau"], 1.0, meta["v_reset"],
                                         meta["use_sig_p"], meta["detach_reset"], sid, 1.0,
-                                        False, 0, 2.0)
+                                        mode == 3, mode if mode in (1, 2) else 0, 2.0)
     elif meta["kind"] == "synaptic":
         y = Fn.EventDrivenSyn.apply(x, W, base, p, b, keep, layer)
     else:
@@ -65,7 +66,7 @@ def run_cuda(meta, inp):
     if b is not None:
         out["dbias"] = b.grad
     torch.cuda.synchronize()
-    return {k: v.cpu() for k, v in out.items()}
+    return {k: v.cpu() for k, v in out.items() if v is not None}
 
 
 def membrane_err(u, u_ref, y, y_ref):

@@ -68,4 +68,6 @@ def mismatch_samples(y, y_ref):
 
 
 def grad_keys(meta, has_bias):
-    return ["dx", "dW", "dd"] + (["dp"] if meta["use_sig_p"] else []) + (["dbias"] if has_bias else [])
+    # the straight-through single-tap variant (mode 3) has no spread gradient
+    sig = meta["use_sig_p"] and meta.get("mode", 0) != 3
+    return ["dx", "dW", "dd"] + (["dp"] if sig else []) + (["dbias"] if has_bias else [])

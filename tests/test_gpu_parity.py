@@ -111,6 +111,45 @@ def test_random_vs_oracle(shape):
     print(rec)
 
 
+@pytest.mark.parametrize("idx", range(12))
+def test_hard_taps_golden(idx):
+    """'triton_ste' (rounded / interpolated taps) and 'triton_approx' axonal variants
+    against the reference's kernels run in those modes (recdel_base.py:350-445)."""
+    from golden_cases import hard_cases
+    from parity import grad_keys
+    case = hard_cases()[idx]
+    meta = case["meta"]
+    got = run_cuda(meta, case["inputs"])
+    ref = case["triton"]
+    ties, clean = compare_scan(got["y"], got["u"], ref["y"], ref["u"])
+    assert clean, f"{ties} near-ties against the reference"
+    compare_grads(got, ref, grad_keys(meta, case["inputs"]["bias"] is not None))
+
+
+HARD_SHAPES = [
+    # mode (1 / 2 triton_ste rounded / interpolated, 3 triton_approx), T, B, N, sigma,
+    # sigp, bias, drop, dmax: the backward paths of the axonal layer (per-sample blocks,
+    # the tensor-core reverse scan, the step-by-step scan of wide layers)
+    (1, 40, 40, 64, 0.5, False, True, False, 16.0),
+    (2, 30, 33, 130, 1.0, True, True, True, 10.0),
+    (3, 30, 33, 130, 1.0, True, False, True, 10.0),
+    (1, 30, 100, 512, 0.0, False, True, True, 25.0),
+    (2, 30, 100, 512, 0.5, False, False, False, 25.0),
+    (3, 30, 100, 512, 0.0, False, True, False, 25.0),
+    (2, 20, 48, 768, 0.5, False, True, True, 20.0),
+    (3, 20, 48, 768, 0.5, False, False, True, 20.0),
+]
+
+
+@pytest.mark.parametrize("shape", HARD_SHAPES, ids=lambda s: f"mode{s[0]}-N{s[3]}-B{s[2]}")
+def test_hard_taps_vs_oracle(shape):
+    mode, T, B, N, sigma, sigp, bias, drop, dmax = shape
+    case = _random_case("axonal", 300 + N + mode, T, B, N, sigma, sigp, bias, drop, dmax)
+    case["meta"]["mode"] = mode
+    rec = check_case(case, name=f"hard_mode{mode}_N{N}_B{B}")
+    print(rec)
+
+
 @pytest.mark.parametrize("T,B,N,K,sigma", [(64, 256, 512, 8, 0.0), (45, 130, 264, 5, 1.0), (16, 40, 96, 8, 0.0)])
 def test_chunked_reverse_scan_matches_stepwise(T, B, N, K, sigma):
     """The chunked reverse scan (tensor-core GEMM per 8-step chunk for the long-lag

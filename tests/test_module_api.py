@@ -138,6 +138,39 @@ def test_reference_forward_versions_are_not_shipped():
         m(torch.zeros(4, 2, cfg.input_size))
 
 
+def test_hard_tap_forward_versions_select_the_variant():
+    """forward_version 'triton_approx' / 'triton_ste' (with config.ste_round_forward)
+    choose the axonal scan's (approx, ste_mode) as delay_layers.py:204-211 and
+    delay_layers_triton.py:60-61 do; other versions run the soft scan."""
+    from types import SimpleNamespace
+    from delrec.delay_layers import _axonal_variant
+    lay = SimpleNamespace(config=SimpleNamespace(), forward_version=None)
+    assert _axonal_variant(lay) == dict(approx=False, ste_mode=0)
+    lay.forward_version = "triton_exact"
+    assert _axonal_variant(lay) == dict(approx=False, ste_mode=0)
+    lay.forward_version = "triton_approx"
+    assert _axonal_variant(lay) == dict(approx=True, ste_mode=0)
+    lay.forward_version = "triton_ste"
+    assert _axonal_variant(lay) == dict(approx=False, ste_mode=1)
+    lay.config.ste_round_forward = False
+    assert _axonal_variant(lay) == dict(approx=False, ste_mode=2)
+
+
+def test_hard_delays_follow_build_lag():
+    """The hard taps as half-width-1 delays: round(d) (ties to even) clamped at 0, or the
+    interpolation position max(d, 0); the host maximum equals the device one."""
+    from delrec.functional import hard_delays
+    d = torch.tensor([0.0, 0.5, 1.5, 2.5, 1.0, -0.7, 3.7, 2.49999])
+    dh, mx = hard_delays(d, float(d.max()), 7, 1)
+    assert dh.tolist() == [0.0, 0.0, 2.0, 2.0, 1.0, 0.0, 4.0, 2.0] and mx == 4.0
+    dh, mx = hard_delays(d, float(d.max()), 7, 2)
+    pos = 1.0 + d
+    lag = torch.floor(pos).clamp(1, 6)
+    assert torch.equal(dh, (lag - 1.0) + (pos - lag).clamp(0, 1))
+    assert mx == float(dh.max())
+    assert torch.equal((1.0 + dh)[d >= 0], pos[d >= 0])
+
+
 def test_feedforward_models_build():
     nw = _nw()
     cfg = mem_config(hidden=[16])

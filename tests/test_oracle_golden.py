@@ -41,6 +41,26 @@ def test_oracle_matches_reference_triton(name):
             assert _rel(out[k], ref[k]) < GRAD_RTOL, f"{k}: rel {_rel(out[k], ref[k]):.2e}"
 
 
+@pytest.mark.parametrize("idx", range(12))
+def test_oracle_hard_taps_match_reference_triton(idx):
+    """The 'triton_ste' (rounded, interpolated) and 'triton_approx' axonal variants:
+    oracle against the reference's kernels in those modes (recdel_base.py:350-445)."""
+    from golden_cases import hard_cases, oracle_run_hard
+    cases = hard_cases()
+    assert len(cases) == 12
+    case = cases[idx]
+    out = oracle_run_hard(case)
+    ref = case["triton"]
+    assert torch.equal(out["y"], ref["y"]), "spike trains differ from the reference kernels"
+    torch.testing.assert_close(out["u"], ref["u"], rtol=1e-5, atol=1e-5)
+    for k in ("dx", "dW", "dd", "dp", "dbias"):
+        if k in ref and (k != "dbias" or case["inputs"]["bias"] is not None):
+            assert k in out, k
+            assert _rel(out[k], ref[k]) < GRAD_RTOL, f"{k}: rel {_rel(out[k], ref[k]):.2e}"
+    if case["meta"]["mode"] == 3:
+        assert "dp" not in ref and "dp" not in out
+
+
 def test_oracle_fp64_agrees_with_fp32():
     """Float64 replay of a case stays within the tolerance used for GPU parity."""
     case = load("hyb_sigma_bias")
