@@ -1,15 +1,15 @@
 """Config objects shaped like the reference's configs/perf_*.py flag classes."""
 
-from delrec.neuron import ATan, LIFNode
-
-
 class _Cfg:
     pass
 
 
-def mem_config(hidden=(64,), bias=False, T=32, B=64, C=8, K=4):
+def mem_config(hidden=(64,), bias=False, T=32, B=64, C=8, K=4, neuron_module=None, surrogate=None):
     """MEM toy (configs/perf_MEM.py) with the SpikingJelly-equivalent
-    neuron of this package."""
+    neuron of this package (or the given neuron class and surrogate)."""
+    if neuron_module is None:
+        from delrec.neuron import ATan, LIFNode
+        neuron_module, surrogate = LIFNode, ATan(alpha=2.0)
     c = _Cfg()
     c.dataset = "MEM"
     c.input_size, c.output_size = C, K
@@ -24,8 +24,8 @@ def mem_config(hidden=(64,), bias=False, T=32, B=64, C=8, K=4):
     c.no_delay_in_first_layer = False
     c.no_delay_in_last_layer = False
     c.no_recurrence_in_last_layer = False
-    c.neuron_module = LIFNode
-    c.surrogate_function = ATan(alpha=2.0)
+    c.neuron_module = neuron_module
+    c.surrogate_function = surrogate
     c.tau, c.decay_input, c.v_threshold, c.v_reset = 2.0, False, 1.0, 0.0
     c.detach_reset = False
     c.step_mode, c.backend, c.store_v_seq = "m", "torch", False

@@ -232,3 +232,29 @@ def test_declared_input_spikes_reach_the_first_projection():
         lins = [m for m in model.layers if type(m).__name__ == "Linear"]
         assert lins[0].binary_input == want
         assert all(m.binary_input is True for m in lins[1:])
+
+
+def _ref_state_dict_cases():
+    import os
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "ref_state_dicts.pt")
+    return torch.load(path, weights_only=False)
+
+
+@pytest.mark.parametrize("idx", range(19))
+def test_state_dict_matches_the_reference_model_zoo(idx):
+    """Every model class of the reference's networks.py, built by the reference's own code
+    (tests/golden/make_state_dicts.py) and by this package for the same config and seed:
+    the same state_dict keys and shapes, and -- for models without a DCLS layer, whose
+    initial values the reference's own code and torch's RNG fully determine -- the same
+    initial values (weights, delays, spreads, biases, BatchNorm, hybrid offsets)."""
+    import sys, os
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+    from make_state_dicts import build
+    case = _ref_state_dict_cases()[idx]
+    m = build(_nw(), mem_config, case["name"], case["overrides"], case["seed"])
+    ours, ref = m.state_dict(), case["state"]
+    assert list(ours) == list(ref), (sorted(set(ours) ^ set(ref)), case["name"])
+    for k, v in ref.items():
+        assert ours[k].shape == v.shape and ours[k].dtype == v.dtype, k
+        if not case["dcls"]:
+            assert torch.equal(ours[k], v), f"{case['name']}: {k} differs"
