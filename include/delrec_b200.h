@@ -7,10 +7,9 @@
  * Every entry point launches on `stream` (a cudaStream_t; NULL = legacy default stream)
  * and returns DELREC_OK or an error code.  Scratch memory is passed in by the caller:
  * query its size with the matching *_workspace function.  Weight gradients, the
- * synaptic lag stack, the projections and the chunked reverse scan run on the library's
- * own tcgen05 GEMM; only the step-by-step forward of axonal layers wider than 512 neurons
- * calls cuBLAS (one IEEE fp32 GEMM per step, on a slice of the workspace; the handle is
- * created on the first such call on each device).
+ * synaptic lag stack, the projections, the chunked reverse scan and the step-by-step
+ * forward and reverse scans of axonal layers wider than 512 neurons run on the library's
+ * own tcgen05 GEMM; the library calls no vendor math library.
  *
  * Reference interfaces replaced (paths are inside ZiyadBekrar/SNN-delays):
  *   delrec_build_mask             triton_kernels/delays.py:13-29, 48-63 (build_mask,

@@ -2,7 +2,6 @@
 // launch planning (block sizes, cluster shapes, shared-memory budgets) and the kernel
 // sequences of each layer forward / backward.  No allocation happens here: all
 // scratch comes from the caller's workspace.
-#include <cublas_v2.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -30,7 +29,6 @@ namespace delrec {
 static constexpr size_t kSmemLimit = 227 * 1024;  // opt-in dynamic shared memory per block
 static constexpr int kSMs = 148;
 static constexpr int kTapsMax = 16;               // widest axonal tap window supported
-static constexpr size_t kCublasWs = 32u << 20;     // cuBLAS workspace slice of a call
 
 static inline int pow2_at_least(int x) {
   int r = 1;
@@ -190,38 +188,79 @@ static int launch_fwd_syn(const FwdArgs& a, const FwdPlan& p, cudaStream_t st) {
   return DELREC_OK;
 }
 
-// Wide axonal layers (N > 512) run their forward step by step: one LIF kernel (which also
-// forms the next step's interpolated spikes as bf16 pieces) and one GEMM per step.
+// Wide axonal layers (N > 512) run their forward step by step: per step one LIF kernel
+// (which also lays out the next step's spike operand) and one tensor-core GEMM
+// rec(t+1) = [Y_0 .. Y_TF-1](t+1) . [W h(0) .. W h(TF-1)]^T over the positive taps, the
+// tap-weighted W in three exact bf16 pieces (linear.cuh).  The GEMM leaves its reduction
+// split's fp32 partials for the LIF kernel, which adds them in a fixed order: no partial
+// sums more than ~1536 piece products, so the tensor core's fp32 accumulation stays
+// within the 1e-5 membrane contract at any width and batch.
 static bool axstep_fwd(const delrec_layer* ly) { return ly->kind == DELREC_AXONAL && ly->N > 512; }
-static int cublas_on(cublasHandle_t* h, void* cws, cudaStream_t st);
-static int gemm_bf16(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k,
-                     const void* A, int lda, const void* B, int ldb, float beta, float* C, int ldc);
-static int gemm_f32_exact(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k,
-                          const float* A, int lda, const float* B, int ldb, float* C, int ldc);
-// Wide axonal layer, one kernel + one fp32 GEMM per step:
-//   k_step_lif_fwd: LIF at t from rec(t), then z(t+1) (B x N, fp32);
-//   rec(t+1) = z(t+1) . W^T on IEEE fp32 (no tensor-core accumulation, whose truncating
-//   fp32 adds over K = N sources drift beyond the 1e-5 membrane contract at N >= 768).
+static constexpr int kFwdStepSplit = 16;
+struct FwdStepPlan {
+  int TF, Kp, BN, ksplit;
+};
+static FwdStepPlan plan_fwd_step(const delrec_layer* ly) {
+  FwdStepPlan p;
+  // positive taps of a triangle of half-width s lie in an open interval of length 2s
+  p.TF = std::max(1, (int)std::ceil(2.0 * (double)ly->s_max - 1e-6));
+  p.Kp = (p.TF * ly->N + 7) / 8 * 8;
+  p.BN = gemm_pick_bn(ly->N);
+  p.ksplit = gemm_pick_ksplit(ly->B, ly->N, p.Kp, 3, 1, 1, p.BN, kFwdStepSplit, 4);
+  // accuracy floor (large batches fill the GPU without splitting): at most ~1536 piece
+  // products per accumulator
+  const int cap = std::max(1, std::min(kFwdStepSplit, 3 * ((p.Kp + 63) / 64) / 4));
+  p.ksplit = std::max(p.ksplit, std::min((3 * p.Kp + 1535) / 1536, cap));
+  return p;
+}
+static size_t fwd_step_ws(const delrec_layer* ly) {
+  const FwdStepPlan p = plan_fwd_step(ly);
+  const size_t N = ly->N, BN = (size_t)ly->B * N;
+  Carve c(nullptr, (size_t)-1);
+  c.take<int2>(N);                                    // positive taps
+  c.take<float>(BN);                                  // v
+  c.take<__nv_bfloat16>((size_t)ly->B * p.Kp);       // spike operand
+  c.take<__nv_bfloat16>(3 * N * p.Kp);               // tap-weighted W pieces
+  c.take<unsigned char>(gemm_partial_bytes(ly->B, ly->N, p.ksplit, 1, true));
+  return c.off;
+}
 static int run_axstep_fwd(const delrec_layer* ly, const FwdArgs& a, const float* W, Carve& c, cudaStream_t st) {
   const int N = ly->N, B = ly->B, T = ly->T;
-  const size_t BN = (size_t)B * N;
-  float* rec = c.take<float>(BN);
+  const FwdStepPlan p = plan_fwd_step(ly);
+  const size_t BN = (size_t)B * N, nk = (size_t)N * p.Kp;
+  int2* fp = c.take<int2>(N);
   float* v = c.take<float>(BN);
-  float* z = c.take<float>(BN);
-  void* cws = c.take<unsigned char>(kCublasWs);
+  __nv_bfloat16* A16 = c.take<__nv_bfloat16>((size_t)B * p.Kp);
+  __nv_bfloat16* Wp = c.take<__nv_bfloat16>(3 * nk);
+  float* part = (float*)c.take<unsigned char>(gemm_partial_bytes(B, N, p.ksplit, 1, true));
   if (!c.ok) return DELREC_ERR_WORKSPACE;
+  k_pos_taps<<<cdiv(N, 256), 256, 0, st>>>(N, a.TAPS, a.tap_l0, a.tap_nt, a.tap_w, p.TF, fp);
+  DR_LAUNCHED();
+  k_wtap_pieces<<<grid_for(nk, 256), 256, 0, st>>>(N, a.TAPS, p.TF, p.Kp, W, a.tap_l0, a.tap_w, fp, Wp, Wp + nk,
+                                                   Wp + 2 * nk);
+  DR_LAUNCHED();
+  DR_CUDA(cudaMemsetAsync(A16, 0, (size_t)B * p.Kp * sizeof(__nv_bfloat16), st));
   k_fill_f32<<<grid_for(BN, 256), 256, 0, st>>>(v, BN, a.lif.v0);
   DR_LAUNCHED();
-  cublasHandle_t h;
-  int rc = cublas_on(&h, cws, st);
+  GemmSide As{}, Ws{};   // K-major bf16 operands: rows x Kp, row stride Kp
+  As.p[0] = A16; As.n = 1; As.rows = B; As.cols = p.Kp; As.ld = p.Kp;
+  Ws.p[0] = Wp; Ws.p[1] = Wp + nk; Ws.p[2] = Wp + 2 * nk; Ws.n = 3;
+  Ws.rows = N; Ws.cols = p.Kp; Ws.ld = p.Kp;
+  GemmArgs g{};
+  g.M = B; g.N = N; g.K = p.Kp; g.nprod = 3; g.nseg = 1;
+  g.pa[0] = g.pa[1] = g.pa[2] = 0;
+  g.pb[0] = 0; g.pb[1] = 1; g.pb[2] = 2;
+  g.ksplit = p.ksplit;
+  g.D = part; g.ldd = N; g.mode = GEMM_PARTIALS;
+  GemmLaunch gl;
+  int rc = gemm_prepare(As, Ws, g, 1, p.BN, part, &gl);   // tensor maps encoded once
   if (rc) return rc;
   for (int t = 0; t < T; ++t) {
-    k_step_lif_fwd<<<grid_for(BN, 256), 256, 0, st>>>(t, T, B, N, a.TAPS, a.x, rec, a.bias, a.keep, a.tap_l0,
-                                                      a.tap_nt, a.tap_w, v, a.y, a.u, z, a.lif);
+    k_step_lif_fwd<<<grid_for(BN, 256), 256, 0, st>>>(t, T, B, N, p.TF, a.x, part, p.ksplit, a.bias, a.keep, fp,
+                                                      v, a.y, a.u, A16, p.Kp, a.lif);
     DR_LAUNCHED();
     if (t + 1 < T) {
-      // column-major: rec (N x B) = W^T-view^T (N x N) . z (N x B); W[i*N + j] target i, source j
-      rc = gemm_f32_exact(h, CUBLAS_OP_T, CUBLAS_OP_N, N, B, N, W, N, z, N, rec, N);
+      rc = gemm_exec(gl, nullptr, st, &g_launches);
       if (rc) return rc;
     }
   }
@@ -235,11 +274,7 @@ static size_t forward_ws(const delrec_layer* ly, int kind, bool allow_step = tru
   c.take<float>(N * N);                             // WT
   if (kind == DELREC_AXONAL) {
     c.take<int>(N); c.take<int>(N); c.take<float>(N * p.TAPS);
-    if (allow_step && axstep_fwd(ly)) {   // step-by-step forward of a wide layer
-      const size_t BN = (size_t)ly->B * N;
-      c.take<float>(BN); c.take<float>(BN); c.take<float>(BN);
-      c.take<unsigned char>(kCublasWs);
-    }
+    if (allow_step && axstep_fwd(ly)) c.take<unsigned char>(fwd_step_ws(ly));   // step-by-step forward
   } else if (kind == DELREC_SYNAPTIC) {
     c.take<float>(N * N);                           // dT
     c.take<int4>(N * N);                            // scatter records
@@ -636,21 +671,6 @@ static SrcPlan plan_src(const delrec_layer* ly) {
 }
 
 // ---- tensor-core dW (dense.cuh) -------------------------------------------------
-static cublasHandle_t g_cublas[64] = {nullptr};
-
-static int cublas_for_device(cublasHandle_t* out) {
-  int dev = 0;
-  DR_CUDA(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64) return DELREC_ERR_UNSUPPORTED;
-  if (!g_cublas[dev]) {
-    if (cublasCreate(&g_cublas[dev]) != CUBLAS_STATUS_SUCCESS) return DELREC_ERR_CUDA;
-  }
-  *out = g_cublas[dev];
-  return DELREC_OK;
-}
-
-static int cublas_on(cublasHandle_t* h, void* cws, cudaStream_t st);
-
 static inline int pad8(int n) { return (n + 7) / 8 * 8; }
 // k_split_bf16_rows launch: a block per row (grid-stride), a thread per 4 columns
 static inline int split_rows_block(int N) { return std::min(256, std::max(32, (cdiv(pad8(N), 4) + 31) / 32 * 32)); }
@@ -826,37 +846,6 @@ static size_t linear_bwd_ws(int M, int K, int N, int xb) {
                                  gemm1_part_bytes(3 * p.Np, p.Kp, M, kLinMaxSplit)));
   return c.off;
 }
-static int gemm_bf16(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k,
-                     const void* A, int lda, const void* B, int ldb, float beta, float* C, int ldc) {
-  const float one = 1.f;
-  const cublasStatus_t e = cublasGemmEx(h, ta, tb, m, n, k, &one, A, CUDA_R_16BF, lda, B, CUDA_R_16BF, ldb,
-                                        &beta, C, CUDA_R_32F, ldc, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
-  if (e != CUBLAS_STATUS_SUCCESS) {
-    fprintf(stderr, "delrec_b200: cublasGemmEx failed (%d)\n", (int)e);
-    return DELREC_ERR_CUDA;
-  }
-  return DELREC_OK;
-}
-// fp32 GEMM with IEEE fp32 products and sums (PEDANTIC: no TF32, no bf16 emulation).
-static int gemm_f32_exact(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k,
-                          const float* A, int lda, const float* B, int ldb, float* C, int ldc) {
-  const float one = 1.f, zero = 0.f;
-  const cublasStatus_t e = cublasGemmEx(h, ta, tb, m, n, k, &one, A, CUDA_R_32F, lda, B, CUDA_R_32F, ldb, &zero,
-                                        C, CUDA_R_32F, ldc, CUBLAS_COMPUTE_32F_PEDANTIC, CUBLAS_GEMM_DEFAULT);
-  if (e != CUBLAS_STATUS_SUCCESS) {
-    fprintf(stderr, "delrec_b200: cublasGemmEx (fp32) failed (%d)\n", (int)e);
-    return DELREC_ERR_CUDA;
-  }
-  return DELREC_OK;
-}
-static int cublas_on(cublasHandle_t* h, void* cws, cudaStream_t st) {
-  int rc = cublas_for_device(h);
-  if (rc) return rc;
-  if (cublasSetStream(*h, st) != CUBLAS_STATUS_SUCCESS) return DELREC_ERR_CUDA;
-  if (cublasSetWorkspace(*h, cws, kCublasWs) != CUBLAS_STATUS_SUCCESS) return DELREC_ERR_CUDA;
-  return DELREC_OK;
-}
-
 static int run_linear_forward(int M, int K, int N, const float* x, const float* W, const float* bias, int xb,
                               float* out, void* ws, size_t wsb, cudaStream_t st) {
   if (M <= 0 || K <= 0 || N <= 0 || !x || !W || !out) return DELREC_ERR_ARG;
@@ -929,14 +918,17 @@ static bool plan_axstep(const delrec_layer* ly, const BwdPlan& bp, bool single_w
   // (the per-step GEMM's operands need 16-byte rows: N a multiple of 8)
   return ly->kind == DELREC_AXONAL && !single_wave_ok && ly->N > 512 && bp.MM == 0 && ly->N % 8 == 0;
 }
-static constexpr int kStepMaxSplit = 2;
+static constexpr int kStepMaxSplit = 16;   // the per-step GEMM fills the GPU by splitting
+static int axstep_ksplit(const delrec_layer* ly) {
+  return gemm_pick_ksplit(ly->B, ly->N, 3 * ly->N, 1, 1, 1, gemm_pick_bn(ly->N), kStepMaxSplit, 4);
+}
 static size_t axstep_ws(const delrec_layer* ly) {
   const size_t N = ly->N, BN = (size_t)ly->B * N;
   Carve c(nullptr, (size_t)-1);
   c.take<float>(BN);                          // lam
   c.take<__nv_bfloat16>(3 * N * N);           // [W_hi; W_lo; W_hi]
   c.take<__nv_bfloat16>(3 * BN);              // [hi | hi | lo] of gr(t)
-  c.take<unsigned char>(gemm1_part_bytes(ly->B, ly->N, 3 * ly->N, kStepMaxSplit));
+  c.take<unsigned char>(gemm_partial_bytes(ly->B, ly->N, axstep_ksplit(ly), 1));
   return c.off;
 }
 static int run_axstep(const delrec_layer* ly, const delrec_lif* lif, const float* gy, const float* u,
@@ -947,7 +939,7 @@ static int run_axstep(const delrec_layer* ly, const delrec_lif* lif, const float
   float* lam = c.take<float>(BN);
   __nv_bfloat16* Wp = c.take<__nv_bfloat16>(3 * nn);
   __nv_bfloat16* g3 = c.take<__nv_bfloat16>(3 * BN);
-  float* part = (float*)c.take<unsigned char>(gemm1_part_bytes(B, N, 3 * N, kStepMaxSplit));
+  float* part = (float*)c.take<unsigned char>(gemm_partial_bytes(B, N, axstep_ksplit(ly), 1));
   if (!c.ok) return DELREC_ERR_WORKSPACE;
   DR_CUDA(cudaMemsetAsync(lam, 0, BN * sizeof(float), st));
   k_split_bf16<<<grid_for(nn, 256), 256, 0, st>>>(W, nn, Wp, Wp + nn);
@@ -957,12 +949,20 @@ static int run_axstep(const delrec_layer* ly, const delrec_lif* lif, const float
   // gz(t)[b][o] = sum_c g3[b][c] Wp[c][o], c over the 3N piece rows (W rows: MN-major operand)
   const GemmSide A = kmajor_operand(g3, B, 3 * N, 3 * N);
   const GemmSide Wm = mnmajor_operand(Wp, 3 * N, N, N);
+  GemmArgs g{};   // one product over K = 3N; the per-step output row block of gz
+  g.M = B; g.N = N; g.K = 3 * N; g.nprod = 1; g.nseg = 1;
+  const int BNt = gemm_pick_bn(N);
+  g.ksplit = axstep_ksplit(ly);
+  g.D = gz; g.ldd = N; g.mode = GEMM_STORE;
+  GemmLaunch gl;
+  int rc = gemm_prepare(A, Wm, g, 1, BNt, part, &gl);   // tensor maps encoded once
+  if (rc) return rc;
   scan_mark(0, st);
   for (int t = T - 1; t >= 0; --t) {
     k_step_lif_bwd<<<grid_for(BN, 256), 256, 0, st>>>(t, T, B, N, TAPS, gy, u, keep, tl0, tnt, tw, gz, lam, dx,
                                                       gr, g3, lk);
     DR_LAUNCHED();
-    const int rc = gemm1(A, Wm, B, N, 3 * N, gz + (size_t)t * BN, N, GEMM_STORE, part, kStepMaxSplit, st);
+    rc = gemm_exec(gl, gz + (size_t)t * BN, st, &g_launches);
     if (rc) return rc;
   }
   scan_mark(1, st);

@@ -27,7 +27,9 @@
 
 namespace delrec {
 
-enum : int { GEMM_STORE = 0, GEMM_ACCUM = 1, GEMM_MASKED = 2 };
+// GEMM_PARTIALS (gemm_run only): the ksplit fp32 partials stay in `part` (split-major,
+// each M x N with row stride N, also for ksplit == 1) for the caller to sum
+enum : int { GEMM_STORE = 0, GEMM_ACCUM = 1, GEMM_MASKED = 2, GEMM_PARTIALS = 3 };
 
 constexpr int kGemmBM = 128, kGemmBK = 64, kGemmThreads = 128, kGemmMaxProd = 6;
 
@@ -372,22 +374,36 @@ struct GemmSide {
 
 // Reduction split: long reductions are cut into parts of at most ~24K products-times-
 // elements, whose fp32 partials are summed outside the tensor core (its accumulator
-// loses accuracy over very long sums), and small grids are split until they fill the
-// GPU.  At most 32 parts and at least 8 stages of 64 per part.
-static int gemm_pick_ksplit(int M, int N, int K, int nprod, int nseg, int nz, int BN, int max_ks = 32) {
+// loses accuracy over very long sums), and grids of fewer tiles than SMs are split
+// further, to the count that costs the fewest waves per unit of work (one CTA per SM:
+// 144 CTAs of 16 tiles x 9 parts run in one wave where 16 x 10 would take two).
+// At most max_ks parts and at least min_stages stages of 64 per part.
+static int gemm_pick_ksplit(int M, int N, int K, int nprod, int nseg, int nz, int BN, int max_ks = 32,
+                            int min_stages = 8) {
   const long long tiles = (long long)((M + kGemmBM - 1) / kGemmBM) * ((N + BN - 1) / BN) * nz;
   const long long steps = (long long)nseg * nprod * ((K + kGemmBK - 1) / kGemmBK);
-  long long ks = (steps * kGemmBK + 24575) / 24576;
-  while (tiles * ks < 148 && ks < max_ks) ++ks;
-  ks = std::min<long long>(ks, std::max<long long>(1, steps / 8));
-  return (int)std::max<long long>(1, std::min<long long>(ks, max_ks));
+  const long long cap = std::max<long long>(1, std::min<long long>(max_ks, steps / min_stages));
+  long long ks = std::min<long long>(cap, std::max<long long>(1, (steps * kGemmBK + 24575) / 24576));
+  if (tiles < 148) {
+    long long best = ks;
+    double best_cost = (double)((tiles * ks + 147) / 148) / (double)ks;
+    for (long long k = ks + 1; k <= cap; ++k) {
+      const double cost = (double)((tiles * k + 147) / 148) / (double)k;
+      if (cost < best_cost - 1e-9) {
+        best = k;
+        best_cost = cost;
+      }
+    }
+    ks = best;
+  }
+  return (int)ks;
 }
 // output columns per tile: the widest of 64 / 128 / 256 that the output needs
 static int gemm_pick_bn(int N) { return N <= 64 ? 64 : (N <= 128 ? 128 : 256); }
 
 // bytes of split-K partials a gemm_run call with these sizes needs from its workspace
-static size_t gemm_partial_bytes(int M, int N, int ksplit, int nz) {
-  return ksplit > 1 ? align256((size_t)M * N * ksplit * nz * sizeof(float)) : 0;
+static size_t gemm_partial_bytes(int M, int N, int ksplit, int nz, bool keep_parts = false) {
+  return (ksplit > 1 || keep_parts) ? align256((size_t)M * N * ksplit * nz * sizeof(float)) : 0;
 }
 
 template <int BN, bool AMN, bool BMN>
@@ -414,11 +430,23 @@ static int gemm_launch_bn(int BN, const CUtensorMap* ma, const CUtensorMap* mb, 
                                : gemm_launch_t<256, AMN, BMN>(ma, mb, g, nz, st));
 }
 
-// D (mode) = sum over products of A-pieces x B-pieces^T, see GemmArgs.  `g` carries the
-// sizes, products, shifts, output and mode; ksplit > 1 runs the reduction in that many
-// parts whose fp32 partials (in `part`, gemm_partial_bytes) are summed in a fixed order.
-static int gemm_run(const GemmSide& A, const GemmSide& B, GemmArgs g, int nz, int BN, float* part, cudaStream_t st,
-                    unsigned long long* launches) {
+// A GEMM with its tensor maps encoded once, for loops that launch the same product many
+// times (the step-by-step scans): gemm_prepare validates and encodes, gemm_exec launches,
+// optionally into another destination D of the same shape.
+struct GemmLaunch {
+  CUtensorMap ma[3], mb[3];
+  GemmArgs g;                 // as launched (D = the partials when the reduction is split)
+  int nz, BN;
+  bool amn, bmn;
+  bool split;                 // partials summed by k_gemm_reduce into D
+  float* D;                   // final destination and its layout / mode
+  long long ldd, d_z;
+  int mode;
+  float* part;
+};
+
+static int gemm_prepare(const GemmSide& A, const GemmSide& B, GemmArgs g, int nz, int BN, float* part,
+                        GemmLaunch* L) {
   if (g.M < 1 || g.N < 1 || g.K < 1 || nz < 1 || g.nprod < 1 || g.nprod > kGemmMaxProd || g.nseg < 1)
     return DELREC_ERR_ARG;
   if (g.ksplit < 1) g.ksplit = 1;
@@ -429,17 +457,20 @@ static int gemm_run(const GemmSide& A, const GemmSide& B, GemmArgs g, int nz, in
   if ((a_contig & 7) || (b_contig & 7)) return DELREC_ERR_ARG;
   for (int p = 0; p < g.nprod; ++p)
     if (g.pa[p] < 0 || g.pa[p] >= A.n || g.pb[p] < 0 || g.pb[p] >= B.n) return DELREC_ERR_ARG;
-  CUtensorMap ma[3], mb[3];
   for (int i = 0; i < 3; ++i) {
     const int ia = i < A.n ? i : 0, ib = i < B.n ? i : 0;
-    if (!tmap_bf16(&ma[i], A.p[ia], A.cols, A.rows, A.ld, A.mn_major ? 64 : kGemmBM)) return DELREC_ERR_ARG;
-    if (!tmap_bf16(&mb[i], B.p[ib], B.cols, B.rows, B.ld, B.mn_major ? 64 : BN)) return DELREC_ERR_ARG;
+    if (!tmap_bf16(&L->ma[i], A.p[ia], A.cols, A.rows, A.ld, A.mn_major ? 64 : kGemmBM)) return DELREC_ERR_ARG;
+    if (!tmap_bf16(&L->mb[i], B.p[ib], B.cols, B.rows, B.ld, B.mn_major ? 64 : BN)) return DELREC_ERR_ARG;
   }
   if (g.spin_ns <= 0) g.spin_ns = 2000000000ll;
-  float* D = g.D;
-  const long long ldd = g.ldd, d_z = g.d_z;
-  const int mode = g.mode;
-  if (g.ksplit > 1) {
+  L->D = g.D;
+  L->ldd = g.ldd;
+  L->d_z = g.d_z;
+  L->mode = g.mode;
+  L->part = part;
+  const bool keep_parts = g.mode == GEMM_PARTIALS;
+  L->split = g.ksplit > 1 && !keep_parts;
+  if (g.ksplit > 1 || keep_parts) {
     if (!part) return DELREC_ERR_WORKSPACE;
     g.D = part;
     g.ldd = g.N;
@@ -447,23 +478,46 @@ static int gemm_run(const GemmSide& A, const GemmSide& B, GemmArgs g, int nz, in
     g.d_z = g.d_split * g.ksplit;
     g.mode = GEMM_STORE;
   }
+  L->g = g;
+  L->nz = nz;
+  L->BN = BN;
+  L->amn = A.mn_major != 0;
+  L->bmn = B.mn_major != 0;
+  return DELREC_OK;
+}
+
+static int gemm_exec(const GemmLaunch& L, float* D, cudaStream_t st, unsigned long long* launches) {
+  GemmArgs g = L.g;
+  float* dst = D ? D : L.D;
+  if (!L.split && L.mode != GEMM_PARTIALS) g.D = dst;
   int rc;
-  if (A.mn_major)
-    rc = B.mn_major ? gemm_launch_bn<true, true>(BN, ma, mb, g, nz, st) : gemm_launch_bn<true, false>(BN, ma, mb, g, nz, st);
+  if (L.amn)
+    rc = L.bmn ? gemm_launch_bn<true, true>(L.BN, L.ma, L.mb, g, L.nz, st)
+               : gemm_launch_bn<true, false>(L.BN, L.ma, L.mb, g, L.nz, st);
   else
-    rc = B.mn_major ? gemm_launch_bn<false, true>(BN, ma, mb, g, nz, st)
-                    : gemm_launch_bn<false, false>(BN, ma, mb, g, nz, st);
+    rc = L.bmn ? gemm_launch_bn<false, true>(L.BN, L.ma, L.mb, g, L.nz, st)
+               : gemm_launch_bn<false, false>(L.BN, L.ma, L.mb, g, L.nz, st);
   if (rc) return rc;
   ++*launches;
-  if (g.ksplit > 1) {
+  if (L.split) {
     const size_t total = (size_t)g.M * g.N;
     int blocks = (int)std::min<size_t>((total + 255) / 256, 148 * 8);
-    k_gemm_reduce<<<dim3(blocks, nz), 256, 0, st>>>(g.M, g.N, g.ksplit, part, g.d_split, g.d_z, g.N, D, ldd, d_z,
-                                                     mode, g.mask, g.ldmask, g.mask_cs, g.z0);
+    k_gemm_reduce<<<dim3(blocks, L.nz), 256, 0, st>>>(g.M, g.N, g.ksplit, L.part, g.d_split, g.d_z, g.N, dst,
+                                                       L.ldd, L.d_z, L.mode, g.mask, g.ldmask, g.mask_cs, g.z0);
     if (cudaGetLastError() != cudaSuccess) return DELREC_ERR_CUDA;
     ++*launches;
   }
   return DELREC_OK;
+}
+
+// D (mode) = sum over products of A-pieces x B-pieces^T, see GemmArgs.  `g` carries the
+// sizes, products, shifts, output and mode; ksplit > 1 runs the reduction in that many
+// parts whose fp32 partials (in `part`, gemm_partial_bytes) are summed in a fixed order.
+static int gemm_run(const GemmSide& A, const GemmSide& B, GemmArgs g, int nz, int BN, float* part, cudaStream_t st,
+                    unsigned long long* launches) {
+  GemmLaunch L;
+  const int rc = gemm_prepare(A, B, g, nz, BN, part, &L);
+  return rc ? rc : gemm_exec(L, nullptr, st, launches);
 }
 
 }  // namespace delrec

@@ -126,23 +126,78 @@ __global__ void k_pack_wt(int N, int K, int Np, int Kp, const float* __restrict_
   }
 }
 
-// One forward step of an axonal layer run step by step (layers too wide for the
-// per-sample scan): for every (b, n),
-//   LIF update at t from rec(t) (the previous step's GEMM; 0 at t = 0),
-//   z(t+1)[b, n] = sum_j w_n[j] y(t+1 - l_j)[b, n]   (n as a source; l_j >= 1),
-// z (B x N, fp32) is the operand of rec(t+1) = z . W^T.
-__global__ void k_step_lif_fwd(int t, int T, int B, int N, int TAPS, const float* __restrict__ x,
-                               const float* __restrict__ rec, const float* __restrict__ bias,
-                               const float* __restrict__ keep, const int* __restrict__ l0,
-                               const int* __restrict__ nt, const float* __restrict__ tw, float* __restrict__ v,
-                               float* __restrict__ y, float* __restrict__ u, float* __restrict__ z, LifK lif) {
+// Wide axonal layers run their forward step by step with rec(t) on the tensor cores as
+//   rec(t)[b, i] = sum_q sum_j Y_q(t)[b, j] * (W[i, j] h_j(q)),
+// where q walks source j's positive taps (weights h_j(q) > 0 of its triangle, in lag
+// order from lag f_j; at most TF of them) and Y_q(t)[b, j] = y(t - f_j - q)[b, j] is a
+// spike (0 or 1, exact in bf16).  W h_j(q) is split into three bf16 pieces whose sum is
+// its fp32 value, so every product is exact and only the additions round.
+
+// (first positive tap's lag, number of positive taps) per source, from the tap tables
+__global__ void k_pos_taps(int N, int TAPS, const int* __restrict__ l0, const int* __restrict__ nt,
+                           const float* __restrict__ tw, int TF, int2* __restrict__ fp) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= N) return;
+  int first = -1, np = 0;
+  for (int q = 0; q < nt[j]; ++q)
+    if (tw[(size_t)j * TAPS + q] > 0.f) {
+      if (first < 0) first = q;
+      ++np;
+    }
+  if (np > TF) { flag_status(ST_LAG_RANGE); np = TF; }
+  fp[j] = make_int2(first < 0 ? 1 : l0[j] + first, np);
+}
+
+// B operand of the step GEMM: row i, column q*N + j = the pieces of fl(W[i, j] h_j(q))
+// (zero for q >= npos_j and in the padding up to Kp)
+__global__ void k_wtap_pieces(int N, int TAPS, int TF, int Kp, const float* __restrict__ W,
+                              const int* __restrict__ l0, const float* __restrict__ tw,
+                              const int2* __restrict__ fp, __nv_bfloat16* __restrict__ p0,
+                              __nv_bfloat16* __restrict__ p1, __nv_bfloat16* __restrict__ p2) {
+  const size_t total = (size_t)N * Kp;
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+    const int i = (int)(e / Kp), c = (int)(e % Kp);
+    const int q = c / N, j = c - q * N;
+    float v = 0.f;
+    if (q < TF && q < fp[j].y) {
+      const int slot = fp[j].x - l0[j] + q;   // index of the tap in j's table
+      v = __fmul_rn(W[(size_t)i * N + j], tw[(size_t)j * TAPS + slot]);
+    }
+    const Pieces3 r = split3(v);
+    p0[e] = r.p[0];
+    p1[e] = r.p[1];
+    p2[e] = r.p[2];
+  }
+}
+
+// One forward step: for every (b, n), rec(t) = the fixed-order sum of the step GEMM's
+// ksplit partials (0 at t = 0), the LIF update at t, and the A operand row of step t+1:
+// A[b, q*N + n] = Y_q(t+1)[b, n] (n as a source).
+__global__ void k_step_lif_fwd(int t, int T, int B, int N, int TF, const float* __restrict__ x,
+                               const float* __restrict__ part, int ksplit, const float* __restrict__ bias,
+                               const float* __restrict__ keep, const int2* __restrict__ fp,
+                               float* __restrict__ v, float* __restrict__ y, float* __restrict__ u,
+                               __nv_bfloat16* __restrict__ A, int Kp, LifK lif) {
   const size_t BN = (size_t)B * N;
+  const __nv_bfloat16 one = __float2bfloat16_rn(1.f), zero = __float2bfloat16_rn(0.f);
   for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < BN; e += (size_t)gridDim.x * blockDim.x) {
     const int n = (int)(e % N);
+    const size_t b = e / N;
     const size_t idx = (size_t)t * BN + e;
+    float rec = 0.f;
+    if (t > 0) {
+      // 4 partials' loads in flight at a time, added in split order
+      int k = 0;
+      for (; k + 4 <= ksplit; k += 4) {
+        const float p0 = __ldcg(part + (size_t)k * BN + e), p1 = __ldcg(part + (size_t)(k + 1) * BN + e);
+        const float p2 = __ldcg(part + (size_t)(k + 2) * BN + e), p3 = __ldcg(part + (size_t)(k + 3) * BN + e);
+        rec = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(rec, p0), p1), p2), p3);
+      }
+      for (; k < ksplit; ++k) rec = __fadd_rn(rec, __ldcg(part + (size_t)k * BN + e));
+    }
     const float bs = bias ? bias[n] : 0.f;
     const float kp = keep ? keep[e] : 1.f;
-    const float r = __fmul_rn(__fadd_rn(t > 0 ? rec[e] : 0.f, bs), kp);
+    const float r = __fmul_rn(__fadd_rn(rec, bs), kp);
     const float av = __fadd_rn(x[idx], r);
     const float uu = lif_charge(v[e], av, lif);
     const bool sp = lif_fire(uu, lif);
@@ -150,16 +205,13 @@ __global__ void k_step_lif_fwd(int t, int T, int B, int N, int TAPS, const float
     y[idx] = sp ? 1.f : 0.f;
     u[idx] = uu;
     if (t + 1 < T) {
-      const int lo = l0[n], cnt = nt[n];
-      float zz = 0.f;
-      for (int j = 0; j < cnt; ++j) {
-        const int l = lo + j;
-        const int ts = t + 1 - l;
-        if (l < 1 || ts < 0) continue;
-        const bool s = l == 1 ? sp : (y[(size_t)ts * BN + e] != 0.f);
-        if (s) zz = __fadd_rn(zz, tw[(size_t)n * TAPS + j]);
+      const int2 f = fp[n];
+      for (int q = 0; q < TF; ++q) {
+        const int ts = t + 1 - (f.x + q);
+        bool s = false;
+        if (q < f.y && ts >= 0) s = ts == t ? sp : (y[(size_t)ts * BN + e] != 0.f);
+        A[b * Kp + (size_t)q * N + n] = s ? one : zero;
       }
-      z[e] = zz;
     }
   }
 }
