@@ -1033,29 +1033,48 @@ static bool tmap_bf16_btn(CUtensorMap* m, const void* base, int N, int T, int B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Programmatic dependent launch (the chunk loop's kernels): the kernel may start while the
+// previous kernel on the stream finishes; its griddepcontrol.wait orders every read of that
+// kernel's results after its completion.
+static cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                                     cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
 template <int KP1>
-static int launch_gz_t(const CUtensorMap* m, const GzArgs& g, int ntiles, cudaStream_t st) {
+static int launch_gz_t(const CUtensorMap* m, const GzArgs& g, int ntiles, cudaStream_t st, bool pdl) {
   auto kern = k_chunk_gz<KP1>;
   int rc = set_smem(kern, kGzSmem);
   if (rc) return rc;
   GzArgs ga = g;
   ga.ntiles = ntiles;
   const int total = cdiv(g.B, kGzSamples) * ntiles;
-  kern<<<std::min(total, kSMs), kGzThreads, kGzSmem, st>>>(m[0], m[1], m[2], m[3], ga);
+  cudaLaunchAttribute attr[1];
+  const cudaLaunchConfig_t cfg = pdl_config(dim3(std::min(total, kSMs)), dim3(kGzThreads), kGzSmem, st, pdl, attr);
+  DR_CUDA(cudaLaunchKernelEx(&cfg, kern, m[0], m[1], m[2], m[3], ga));
   DR_LAUNCHED();
   return DELREC_OK;
 }
-static int launch_gz(int KP1, const CUtensorMap* m, const GzArgs& g, int ntiles, cudaStream_t st) {
+static int launch_gz(int KP1, const CUtensorMap* m, const GzArgs& g, int ntiles, cudaStream_t st, bool pdl) {
   switch (KP1) {
-    case 1: return launch_gz_t<1>(m, g, ntiles, st);
-    case 2: return launch_gz_t<2>(m, g, ntiles, st);
-    case 3: return launch_gz_t<3>(m, g, ntiles, st);
-    case 4: return launch_gz_t<4>(m, g, ntiles, st);
-    case 5: return launch_gz_t<5>(m, g, ntiles, st);
-    case 6: return launch_gz_t<6>(m, g, ntiles, st);
-    case 7: return launch_gz_t<7>(m, g, ntiles, st);
-    case 8: return launch_gz_t<8>(m, g, ntiles, st);
-    case 9: return launch_gz_t<9>(m, g, ntiles, st);
+    case 1: return launch_gz_t<1>(m, g, ntiles, st, pdl);
+    case 2: return launch_gz_t<2>(m, g, ntiles, st, pdl);
+    case 3: return launch_gz_t<3>(m, g, ntiles, st, pdl);
+    case 4: return launch_gz_t<4>(m, g, ntiles, st, pdl);
+    case 5: return launch_gz_t<5>(m, g, ntiles, st, pdl);
+    case 6: return launch_gz_t<6>(m, g, ntiles, st, pdl);
+    case 7: return launch_gz_t<7>(m, g, ntiles, st, pdl);
+    case 8: return launch_gz_t<8>(m, g, ntiles, st, pdl);
+    case 9: return launch_gz_t<9>(m, g, ntiles, st, pdl);
     default: return DELREC_ERR_UNSUPPORTED;
   }
 }
@@ -1140,8 +1159,11 @@ static int run_chunked(const delrec_layer* ly, const Hyb64Plan& h64, const Chunk
     scan_mark(0, st, 1);
     if (local) {
       LocArgs la{a, sh_idx, sh_w, c_idx, c_w, pairs, pcnt, pcnt + 8, lecap};
-      lkern<<<cdiv(B, S), lnth, lsmem, st>>>(la);
-      DR_CUDA(cudaGetLastError());
+      // the first chunk follows the kernels that build its tables: an ordinary launch
+      cudaLaunchAttribute attr[1];
+      const cudaLaunchConfig_t cfg =
+          pdl_config(dim3(cdiv(B, S)), dim3(lnth), lsmem, st, ch < cp.nchunks - 1 && !g_scan_timing, attr);
+      DR_CUDA(cudaLaunchKernelEx(&cfg, lkern, la));
     } else {
       ChunkArgs ac = a;
       void* args[] = {(void*)&ac};
@@ -1152,7 +1174,7 @@ static int run_chunked(const delrec_layer* ly, const Hyb64Plan& h64, const Chunk
     ++g_launches;
     g.t0 = a.t0;
     scan_mark(0, st, 2);
-    rc = launch_gz(cp.KP1, maps, g, cp.ntiles, st);
+    rc = launch_gz(cp.KP1, maps, g, cp.ntiles, st, local && !g_scan_timing);
     scan_mark(1, st, 2);
     if (rc) return rc;
   }

@@ -436,6 +436,11 @@ __global__ void __launch_bounds__(kGzThreads, 1)
   tc_fence_after();
   const uint32_t tmem = s_tmem;
   volatile int* abort = &s_abort;
+  // Launched as a programmatic dependent of the chunk's step kernel, the set-up above
+  // overlaps that kernel's tail; the gr pieces and gz are read and added only below.
+  // Without the launch attribute both instructions do nothing.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
     if (lane == 0) {

@@ -250,6 +250,12 @@ __global__ void __launch_bounds__(NTH, 1) k_bwd_chunk_local(LocArgs la) {
     for (int v = tid; v < n16 * 2; v += NTH) sw4[v] = gw[v];
   }
   __syncthreads();
+  // Launched as a programmatic dependent of the previous chunk's GEMM, the set-up above
+  // (static tables written before the first chunk) overlaps that GEMM's last tiles; lam
+  // and gz below are what the previous kernels wrote.  Without the launch attribute both
+  // instructions do nothing.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // pairs p = tid + k * NTH: sample bl = p / N, source o = p % N
   int po[PPT], pb[PPT];
