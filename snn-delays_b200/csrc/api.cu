@@ -188,6 +188,23 @@ static int launch_fwd_syn(const FwdArgs& a, const FwdPlan& p, cudaStream_t st) {
   return DELREC_OK;
 }
 
+// Programmatic dependent launch (the chunk loop's and the step loops' kernels): the kernel
+// may start while the previous kernel on the stream finishes; its griddepcontrol.wait
+// orders every read of that kernel's results after its completion.
+static cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                                     cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
 // Wide axonal layers (N > 512) run their forward step by step: per step one LIF kernel
 // (which also lays out the next step's spike operand) and one tensor-core GEMM
 // rec(t+1) = [Y_0 .. Y_TF-1](t+1) . [W h(0) .. W h(TF-1)]^T over the positive taps, the
@@ -255,12 +272,15 @@ static int run_axstep_fwd(const delrec_layer* ly, const FwdArgs& a, const float*
   GemmLaunch gl;
   int rc = gemm_prepare(As, Ws, g, 1, p.BN, part, &gl);   // tensor maps encoded once
   if (rc) return rc;
+  // every launch after the first is a programmatic dependent of the one before it
   for (int t = 0; t < T; ++t) {
-    k_step_lif_fwd<<<grid_for(BN, 256), 256, 0, st>>>(t, T, B, N, p.TF, a.x, part, p.ksplit, a.bias, a.keep, fp,
-                                                      v, a.y, a.u, A16, p.Kp, a.lif);
+    cudaLaunchAttribute attr[1];
+    const cudaLaunchConfig_t cfg = pdl_config(dim3(grid_for(BN, 256)), dim3(256), 0, st, t > 0, attr);
+    DR_CUDA(cudaLaunchKernelEx(&cfg, k_step_lif_fwd, t, T, B, N, p.TF, a.x, (const float*)part, p.ksplit, a.bias,
+                               a.keep, (const int2*)fp, v, a.y, a.u, A16, p.Kp, a.lif));
     DR_LAUNCHED();
     if (t + 1 < T) {
-      rc = gemm_exec(gl, nullptr, st, &g_launches);
+      rc = gemm_exec(gl, nullptr, st, &g_launches, true);
       if (rc) return rc;
     }
   }
@@ -785,15 +805,27 @@ static int syn_cstack(const delrec_layer* ly, const float* gr, const float* y, c
 
 // ---- feedforward projection on tensor cores (linear.cuh) ------------------------
 struct LinPlan {
-  int Kp, Np, pf, nbx;   // padded widths, forward blocks, backward x pieces
+  int Kp, Np, nbx;       // padded widths, x pieces (1 for spikes, else 3)
 };
 static LinPlan plan_linear(int K, int N, int x_binary) {
   LinPlan p;
   p.Kp = (K + 1 + 7) / 8 * 8;
   p.Np = (N + 7) / 8 * 8;
-  p.pf = x_binary ? 3 : 6;
   p.nbx = x_binary ? 1 : 3;
   return p;
+}
+// The piece products with i + j <= 2 of two 3-piece operands (or the 3 products of a
+// 1-piece spike operand with the 3 pieces of the other), each operand's pieces stored once
+static void lin_products(GemmArgs* g, int a_pieces) {
+  static const int pa6[6] = {0, 1, 2, 0, 1, 0}, pb6[6] = {0, 0, 0, 1, 1, 2};
+  g->nprod = a_pieces == 1 ? 3 : 6;
+  for (int q = 0; q < g->nprod; ++q) {
+    g->pa[q] = a_pieces == 1 ? 0 : pa6[q];
+    g->pb[q] = a_pieces == 1 ? q : pb6[q];
+  }
+}
+static int lin_ksplit(int M, int N, int K, int nprod) {
+  return gemm_pick_ksplit(M, N, K, nprod, 1, 1, gemm_pick_bn(N), 8);
 }
 // K-major bf16 operand: rows x cols, row stride ld
 static GemmSide kmajor_operand(const void* p, long long rows, long long cols, long long ld) {
@@ -830,19 +862,19 @@ static constexpr int kLinMaxSplit = 8;
 static size_t linear_fwd_ws(int M, int K, int N, int xb) {
   const LinPlan p = plan_linear(K, N, xb);
   Carve c(nullptr, (size_t)-1);
-  c.take<__nv_bfloat16>((size_t)M * p.pf * p.Kp);
-  c.take<__nv_bfloat16>((size_t)N * p.pf * p.Kp);
-  c.take<unsigned char>(gemm1_part_bytes(M, N, p.pf * p.Kp, kLinMaxSplit));
+  c.take<__nv_bfloat16>((size_t)M * p.nbx * p.Kp);
+  c.take<__nv_bfloat16>((size_t)N * 3 * p.Kp);
+  c.take<unsigned char>(gemm_partial_bytes(M, N, lin_ksplit(M, N, p.Kp, p.nbx == 1 ? 3 : 6), 1));
   return c.off;
 }
 static size_t linear_bwd_ws(int M, int K, int N, int xb) {
   const LinPlan p = plan_linear(K, N, xb);
   Carve c(nullptr, (size_t)-1);
   c.take<__nv_bfloat16>((size_t)M * p.nbx * p.Kp);
-  c.take<__nv_bfloat16>((size_t)M * 6 * p.Np);
-  c.take<__nv_bfloat16>((size_t)6 * p.Np * p.Kp);
+  c.take<__nv_bfloat16>((size_t)M * 3 * p.Np);
+  c.take<__nv_bfloat16>((size_t)3 * p.Np * p.Kp);
   c.take<float>((size_t)3 * p.Np * p.Kp);
-  c.take<unsigned char>(std::max(gemm1_part_bytes(M, K, 6 * p.Np, kLinMaxSplit),
+  c.take<unsigned char>(std::max(gemm_partial_bytes(M, K, lin_ksplit(M, K, p.Np, 6), 1),
                                  gemm1_part_bytes(3 * p.Np, p.Kp, M, kLinMaxSplit)));
   return c.off;
 }
@@ -852,20 +884,32 @@ static int run_linear_forward(int M, int K, int N, const float* x, const float* 
   if (((uintptr_t)ws & 255) != 0 || wsb < linear_fwd_ws(M, K, N, xb)) return DELREC_ERR_WORKSPACE;
   const LinPlan p = plan_linear(K, N, xb);
   Carve c(ws, wsb);
-  __nv_bfloat16* X = c.take<__nv_bfloat16>((size_t)M * p.pf * p.Kp);
-  __nv_bfloat16* Wp = c.take<__nv_bfloat16>((size_t)N * p.pf * p.Kp);
-  float* part = (float*)c.take<unsigned char>(gemm1_part_bytes(M, N, p.pf * p.Kp, kLinMaxSplit));
+  __nv_bfloat16* X = c.take<__nv_bfloat16>((size_t)M * p.nbx * p.Kp);
+  __nv_bfloat16* Wp = c.take<__nv_bfloat16>((size_t)N * 3 * p.Kp);
+  const int nprod = p.nbx == 1 ? 3 : 6, ks = lin_ksplit(M, N, p.Kp, nprod);
+  float* part = (float*)c.take<unsigned char>(gemm_partial_bytes(M, N, ks, 1));
   if (!c.ok) return DELREC_ERR_WORKSPACE;
-  k_pack_rows<<<grid_for((size_t)M * p.Kp / 8, 256), 256, 0, st>>>(M, K, p.Kp, x, K, nullptr, 1, p.pf,
-                                                                   xb ? kPatSpike3 : kPatReal6, xb, X);
+  // rows [x0 (x1 x2)] and [W0 W1 W2], the ones / bias column at K
+  k_pack_rows<<<grid_for((size_t)M * p.Kp / 8, 256), 256, 0, st>>>(M, K, p.Kp, x, K, nullptr, 1, p.nbx,
+                                                                   kPatDistinct3, xb, X);
   DR_LAUNCHED();
-  k_pack_rows<<<grid_for((size_t)N * p.Kp / 8, 256), 256, 0, st>>>(N, K, p.Kp, W, K, bias, 0, p.pf,
-                                                                   xb ? kPatW3 : kPatW6, 0, Wp);
+  k_pack_rows<<<grid_for((size_t)N * p.Kp / 8, 256), 256, 0, st>>>(N, K, p.Kp, W, K, bias, 0, 3, kPatDistinct3, 0,
+                                                                   Wp);
   DR_LAUNCHED();
-  // out[m][n] = sum_c X'[m][c] W'[n][c]: the piece products laid along the reduction
-  const int Kt = p.pf * p.Kp;
-  return gemm1(kmajor_operand(X, M, Kt, Kt), kmajor_operand(Wp, N, Kt, Kt), M, N, Kt, out, N, GEMM_STORE, part,
-               kLinMaxSplit, st);
+  // out[m][n] = sum over the piece products of X_i[m][.] W_j[n][.]
+  GemmSide A{}, Bw{};
+  for (int i = 0; i < 3; ++i) {
+    A.p[i] = X + (size_t)std::min(i, p.nbx - 1) * p.Kp;
+    Bw.p[i] = Wp + (size_t)i * p.Kp;
+  }
+  A.n = p.nbx; A.rows = M; A.cols = p.Kp; A.ld = (long long)p.nbx * p.Kp;
+  Bw.n = 3; Bw.rows = N; Bw.cols = p.Kp; Bw.ld = 3LL * p.Kp;
+  GemmArgs g{};
+  g.M = M; g.N = N; g.K = p.Kp; g.nseg = 1;
+  lin_products(&g, p.nbx);
+  g.ksplit = ks;
+  g.D = out; g.ldd = N; g.mode = GEMM_STORE;
+  return gemm_run(A, Bw, g, 1, gemm_pick_bn(N), part, st, &g_launches);
 }
 
 static int run_linear_backward(int M, int K, int N, const float* x, const float* W, const float* gout, int xb,
@@ -875,24 +919,36 @@ static int run_linear_backward(int M, int K, int N, const float* x, const float*
   const LinPlan p = plan_linear(K, N, xb);
   Carve c(ws, wsb);
   __nv_bfloat16* X = c.take<__nv_bfloat16>((size_t)M * p.nbx * p.Kp);
-  __nv_bfloat16* G = c.take<__nv_bfloat16>((size_t)M * 6 * p.Np);
-  __nv_bfloat16* Wt = c.take<__nv_bfloat16>((size_t)6 * p.Np * p.Kp);
+  __nv_bfloat16* G = c.take<__nv_bfloat16>((size_t)M * 3 * p.Np);
+  __nv_bfloat16* Wt = c.take<__nv_bfloat16>((size_t)3 * p.Np * p.Kp);
   float* D = c.take<float>((size_t)3 * p.Np * p.Kp);
-  float* part = (float*)c.take<unsigned char>(std::max(gemm1_part_bytes(M, K, 6 * p.Np, kLinMaxSplit),
+  const int ksx = lin_ksplit(M, K, p.Np, 6);
+  float* part = (float*)c.take<unsigned char>(std::max(gemm_partial_bytes(M, K, ksx, 1),
                                                        gemm1_part_bytes(3 * p.Np, p.Kp, M, kLinMaxSplit)));
   if (!c.ok) return DELREC_ERR_WORKSPACE;
-  // G' = [g0 g1 g2 g0 g1 g0]; the weight-gradient products read only its first three blocks,
-  // so without dx the last three are not written (gb: blocks per row of G')
-  const int gb = dx ? 6 : 3;
-  k_pack_rows<<<grid_for((size_t)M * p.Np / 8, 256), 256, 0, st>>>(M, N, p.Np, gout, N, nullptr, 0, gb, kPatReal6,
-                                                                   0, G);
+  // G = [g0 g1 g2] per row (gb blocks): the three pieces of gout, each stored once
+  const int gb = 3;
+  k_pack_rows<<<grid_for((size_t)M * p.Np / 8, 256), 256, 0, st>>>(M, N, p.Np, gout, N, nullptr, 0, gb,
+                                                                   kPatDistinct3, 0, G);
   DR_LAUNCHED();
   if (dx) {
-    k_pack_wt<<<grid_for((size_t)p.Np * p.Kp / 8, 256), 256, 0, st>>>(N, K, p.Np, p.Kp, W, kPatW6, 6, Wt);
+    k_pack_wt<<<grid_for((size_t)p.Np * p.Kp / 8, 256), 256, 0, st>>>(N, K, p.Np, p.Kp, W, kPatDistinct3, 3, Wt);
     DR_LAUNCHED();
-    // dx[m][k] = sum_c G'[m][c] W''[c][k]  (W'' rows along the reduction: MN-major)
-    const int rc = gemm1(kmajor_operand(G, M, 6 * p.Np, 6 * p.Np), mnmajor_operand(Wt, 6 * p.Np, K, p.Kp), M, K,
-                         6 * p.Np, dx, K, GEMM_STORE, part, kLinMaxSplit, st);
+    // dx[m][k] = sum over the piece products of G_i[m][.] W_j[.][k]  (W pieces: rows along
+    // the reduction, MN-major)
+    GemmSide A{}, Bw{};
+    for (int i = 0; i < 3; ++i) {
+      A.p[i] = G + (size_t)i * p.Np;
+      Bw.p[i] = Wt + (size_t)i * p.Np * p.Kp;
+    }
+    A.n = 3; A.rows = M; A.cols = p.Np; A.ld = 3LL * p.Np;
+    Bw.n = 3; Bw.rows = p.Np; Bw.cols = K; Bw.ld = p.Kp; Bw.mn_major = 1;
+    GemmArgs g{};
+    g.M = M; g.N = K; g.K = p.Np; g.nseg = 1;
+    lin_products(&g, 3);
+    g.ksplit = ksx;
+    g.D = dx; g.ldd = K; g.mode = GEMM_STORE;
+    const int rc = gemm_run(A, Bw, g, 1, gemm_pick_bn(K), part, st, &g_launches);
     if (rc) return rc;
   }
   if (dW || dbias) {
@@ -958,11 +1014,14 @@ static int run_axstep(const delrec_layer* ly, const delrec_lif* lif, const float
   int rc = gemm_prepare(A, Wm, g, 1, BNt, part, &gl);   // tensor maps encoded once
   if (rc) return rc;
   scan_mark(0, st);
+  // every launch after the first is a programmatic dependent of the one before it
   for (int t = T - 1; t >= 0; --t) {
-    k_step_lif_bwd<<<grid_for(BN, 256), 256, 0, st>>>(t, T, B, N, TAPS, gy, u, keep, tl0, tnt, tw, gz, lam, dx,
-                                                      gr, g3, lk);
+    cudaLaunchAttribute attr[1];
+    const cudaLaunchConfig_t cfg = pdl_config(dim3(grid_for(BN, 256)), dim3(256), 0, st, t < T - 1, attr);
+    DR_CUDA(cudaLaunchKernelEx(&cfg, k_step_lif_bwd, t, T, B, N, TAPS, gy, u, keep, tl0, tnt, tw, (const float*)gz,
+                               lam, dx, gr, g3, lk));
     DR_LAUNCHED();
-    rc = gemm_exec(gl, gz + (size_t)t * BN, st, &g_launches);
+    rc = gemm_exec(gl, gz + (size_t)t * BN, st, &g_launches, true);
     if (rc) return rc;
   }
   scan_mark(1, st);
@@ -1031,23 +1090,6 @@ static bool tmap_bf16_btn(CUtensorMap* m, const void* base, int N, int T, int B,
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-// Programmatic dependent launch (the chunk loop's kernels): the kernel may start while the
-// previous kernel on the stream finishes; its griddepcontrol.wait orders every read of that
-// kernel's results after its completion.
-static cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
-                                     cudaLaunchAttribute* attr) {
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cfg;
 }
 
 template <int KP1>

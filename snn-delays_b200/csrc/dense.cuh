@@ -76,6 +76,8 @@ __global__ void k_step_lif_bwd(int t, int T, int B, int N, int TAPS, const float
                                const float* __restrict__ tw, const float* __restrict__ gz,
                                float* __restrict__ lam, float* __restrict__ dx, float* __restrict__ gr,
                                __nv_bfloat16* __restrict__ g3, LifK lif) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");   // no-op unless launched as a dependent
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const size_t BN = (size_t)B * N;
   for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < BN; e += (size_t)gridDim.x * blockDim.x) {
     const int o = (int)(e % N), b = (int)(e / N);

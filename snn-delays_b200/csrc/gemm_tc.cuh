@@ -206,6 +206,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem = s_tmem;
   volatile int* abort = &s_abort;
+  // Launched as a programmatic dependent (the step-by-step scans), the set-up above overlaps
+  // the previous kernel's tail; operands are read only below.  Without the launch
+  // attribute both instructions do nothing.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (j1 > j0) {
     if (warp == 0 && lane == 0) {
@@ -311,6 +316,8 @@ __global__ void k_gemm_reduce(int M, int N, int ksplit, const float* __restrict_
                               long long p_z, long long ldp, float* __restrict__ D, long long ldd, long long d_z,
                               int mode, const uint8_t* __restrict__ mask, long long ldmask, long long mask_cs,
                               int z0) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");   // no-op unless launched as a dependent
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int zi = blockIdx.y, z = z0 + zi;
   const size_t total = (size_t)M * N;
   for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
@@ -407,7 +414,8 @@ static size_t gemm_partial_bytes(int M, int N, int ksplit, int nz, bool keep_par
 }
 
 template <int BN, bool AMN, bool BMN>
-static int gemm_launch_t(const CUtensorMap* ma, const CUtensorMap* mb, const GemmArgs& g, int nz, cudaStream_t st) {
+static int gemm_launch_t(const CUtensorMap* ma, const CUtensorMap* mb, const GemmArgs& g, int nz, cudaStream_t st,
+                         bool pdl) {
   static bool attr_set[64] = {false};   // per device
   const size_t smem = gemm_smem_bytes(BN);
   int dev = 0;
@@ -419,15 +427,25 @@ static int gemm_launch_t(const CUtensorMap* ma, const CUtensorMap* mb, const Gem
     attr_set[dev] = true;
   }
   const int tiles = ((g.M + kGemmBM - 1) / kGemmBM) * ((g.N + BN - 1) / BN);
-  kern<<<dim3(tiles, g.ksplit, nz), kGemmThreads, smem, st>>>(ma[0], ma[1], ma[2], mb[0], mb[1], mb[2], g);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(tiles, g.ksplit, nz);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, ma[0], ma[1], ma[2], mb[0], mb[1], mb[2], g) != cudaSuccess) return DELREC_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? DELREC_OK : DELREC_ERR_CUDA;
 }
 template <bool AMN, bool BMN>
 static int gemm_launch_bn(int BN, const CUtensorMap* ma, const CUtensorMap* mb, const GemmArgs& g, int nz,
-                          cudaStream_t st) {
-  return BN == 64 ? gemm_launch_t<64, AMN, BMN>(ma, mb, g, nz, st)
-                  : (BN == 128 ? gemm_launch_t<128, AMN, BMN>(ma, mb, g, nz, st)
-                               : gemm_launch_t<256, AMN, BMN>(ma, mb, g, nz, st));
+                          cudaStream_t st, bool pdl = false) {
+  return BN == 64 ? gemm_launch_t<64, AMN, BMN>(ma, mb, g, nz, st, pdl)
+                  : (BN == 128 ? gemm_launch_t<128, AMN, BMN>(ma, mb, g, nz, st, pdl)
+                               : gemm_launch_t<256, AMN, BMN>(ma, mb, g, nz, st, pdl));
 }
 
 // A GEMM with its tensor maps encoded once, for loops that launch the same product many
@@ -486,25 +504,38 @@ static int gemm_prepare(const GemmSide& A, const GemmSide& B, GemmArgs g, int nz
   return DELREC_OK;
 }
 
-static int gemm_exec(const GemmLaunch& L, float* D, cudaStream_t st, unsigned long long* launches) {
+// pdl: the GEMM (and its reduce) are launched as programmatic dependents of the work
+// before them on the stream (both wait for it before reading anything)
+static int gemm_exec(const GemmLaunch& L, float* D, cudaStream_t st, unsigned long long* launches,
+                     bool pdl = false) {
   GemmArgs g = L.g;
   float* dst = D ? D : L.D;
   if (!L.split && L.mode != GEMM_PARTIALS) g.D = dst;
   int rc;
   if (L.amn)
-    rc = L.bmn ? gemm_launch_bn<true, true>(L.BN, L.ma, L.mb, g, L.nz, st)
-               : gemm_launch_bn<true, false>(L.BN, L.ma, L.mb, g, L.nz, st);
+    rc = L.bmn ? gemm_launch_bn<true, true>(L.BN, L.ma, L.mb, g, L.nz, st, pdl)
+               : gemm_launch_bn<true, false>(L.BN, L.ma, L.mb, g, L.nz, st, pdl);
   else
-    rc = L.bmn ? gemm_launch_bn<false, true>(L.BN, L.ma, L.mb, g, L.nz, st)
-               : gemm_launch_bn<false, false>(L.BN, L.ma, L.mb, g, L.nz, st);
+    rc = L.bmn ? gemm_launch_bn<false, true>(L.BN, L.ma, L.mb, g, L.nz, st, pdl)
+               : gemm_launch_bn<false, false>(L.BN, L.ma, L.mb, g, L.nz, st, pdl);
   if (rc) return rc;
   ++*launches;
   if (L.split) {
     const size_t total = (size_t)g.M * g.N;
     int blocks = (int)std::min<size_t>((total + 255) / 256, 148 * 8);
-    k_gemm_reduce<<<dim3(blocks, L.nz), 256, 0, st>>>(g.M, g.N, g.ksplit, L.part, g.d_split, g.d_z, g.N, dst,
-                                                       L.ldd, L.d_z, L.mode, g.mask, g.ldmask, g.mask_cs, g.z0);
-    if (cudaGetLastError() != cudaSuccess) return DELREC_ERR_CUDA;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(blocks, L.nz);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, k_gemm_reduce, g.M, g.N, g.ksplit, (const float*)L.part, (long long)g.d_split,
+                           (long long)g.d_z, (long long)g.N, dst, (long long)L.ldd, (long long)L.d_z, L.mode,
+                           g.mask, (long long)g.ldmask, (long long)g.mask_cs, g.z0) != cudaSuccess)
+      return DELREC_ERR_CUDA;
     ++*launches;
   }
   return DELREC_OK;

@@ -8,16 +8,16 @@
 // 2^-24 relative), accumulated in fp32 by the tensor cores.  Operands in {0, 1} (spike
 // trains) are exact in one bf16 piece, so a product with them needs three products only.
 //
-// The piece products of one output are laid side by side along the reduction dimension,
-// so each is ONE plain GEMM (cuBLAS, bf16 in, fp32 accumulate):
-//   forward   out (M,N) = X'(M, P*Kp) . W'(N, P*Kp)^T
-//   real x:   X' blocks [x0 x1 x2 x0 x1 x0], W' blocks [W0 W0 W0 W1 W1 W2]  (P = 6)
-//   spikes:   X' blocks [x  x  x ],          W' blocks [W0 W1 W2]           (P = 3)
-//   the bias rides along as column K of every block: 1 in the x0 (spike: x) blocks, the
-//   matching bias piece in W', so the GEMM returns x W^T + bias;
-//   input gradient  dx (M,K) = G'(M, 6*Np) . W''(6*Np, Kp),
-//     G' blocks [g0 g1 g2 g0 g1 g0] of gout, W'' row blocks [W0 W0 W0 W1 W1 W2];
-//   weight gradient D (3*Np, Kp) = sum_a x_a^T G'[:, 0 : (3-a)*Np]  (one GEMM for spikes,
+// Each operand's pieces are stored once, side by side in its rows ([x0 x1 x2], or [x]
+// for spikes; [W0 W1 W2]), and ONE launch of the library's tcgen05 GEMM sums the piece
+// products, each product pairing a piece of one operand with a piece of the other
+// (gemm_tc.cuh: GemmArgs pa / pb):
+//   forward   out (M,N) = sum x_i . W_j^T over i + j <= 2 (real x: 6 products) or over
+//             j (spikes: 3 products); the bias rides along as column K: 1 in x0 (the
+//             pieces of 1 are 1, 0, 0), the bias pieces in W0..W2;
+//   input gradient  dx (M,K) = sum g_i . W_j over i + j <= 2, with G = [g0 g1 g2] of gout
+//     and the pieces of W stored transposed (their rows along the reduction);
+//   weight gradient D (3*Np, Kp) = sum_a x_a^T G[:, 0 : (3-a)*Np]  (one GEMM for spikes,
 //     three for real x), then dW = D[0:N] + D[Np:Np+N] + D[2Np:2Np+N] and dbias = its
 //     column K.
 // Kp = roundup(K + 1, 8) and Np = roundup(N, 8) keep every bf16 row 16-byte aligned.
@@ -42,11 +42,7 @@ __device__ __forceinline__ Pieces3 split3(float v) {
   return r;
 }
 
-// Block patterns (piece index of block q), two bits per block.
-constexpr unsigned kPatReal6 = (0u << 0) | (1u << 2) | (2u << 4) | (0u << 6) | (1u << 8) | (0u << 10);
-constexpr unsigned kPatW6 = (0u << 0) | (0u << 2) | (0u << 4) | (1u << 6) | (1u << 8) | (2u << 10);
-constexpr unsigned kPatSpike3 = 0u;                                  // x, x, x
-constexpr unsigned kPatW3 = (0u << 0) | (1u << 2) | (2u << 4);      // W0, W1, W2
+// Block pattern (piece index of block q, two bits per block): pieces 0, 1, 2 in order.
 constexpr unsigned kPatDistinct3 = (0u << 0) | (1u << 2) | (2u << 4);
 
 // out[r][q*Wd + c] = piece pat(q) of
@@ -100,7 +96,7 @@ __global__ void k_pack_rows(int R, int K, int Wd, const float* __restrict__ src,
   }
 }
 
-// W''[q*Np + n][c] = piece pat(q) of W[n*K + c] (c < K, n < N), else 0.   (6*Np rows, Kp cols)
+// W''[q*Np + n][c] = piece pat(q) of W[n*K + c] (c < K, n < N), else 0.   (nb*Np rows, Kp cols)
 __global__ void k_pack_wt(int N, int K, int Np, int Kp, const float* __restrict__ W, unsigned pat, int nb,
                           __nv_bfloat16* __restrict__ out) {
   const int groups = Kp >> 3;
@@ -178,6 +174,8 @@ __global__ void k_step_lif_fwd(int t, int T, int B, int N, int TF, const float* 
                                const float* __restrict__ keep, const int2* __restrict__ fp,
                                float* __restrict__ v, float* __restrict__ y, float* __restrict__ u,
                                __nv_bfloat16* __restrict__ A, int Kp, LifK lif) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");   // no-op unless launched as a dependent
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const size_t BN = (size_t)B * N;
   const __nv_bfloat16 one = __float2bfloat16_rn(1.f), zero = __float2bfloat16_rn(0.f);
   for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < BN; e += (size_t)gridDim.x * blockDim.x) {
