@@ -99,6 +99,12 @@ def loss_fn(out, labels):
     return torch.nn.functional.cross_entropy(out.sum(0), labels)
 
 
+def model_loss(model, x, labels):
+    """The same loss as loss_fn(model(x), labels): the readout summed over time, fused in
+    the library (forward_time_summed) instead of forming the (T,B,C) readout."""
+    return torch.nn.functional.cross_entropy(model.forward_time_summed(x), labels)
+
+
 # ----------------------------------------------------------------------------------
 # clocks sampled during the timed region
 # ----------------------------------------------------------------------------------
@@ -418,8 +424,7 @@ def main():
 
     def step(xb, lb):
         opt.zero_grad(set_to_none=True)
-        out = model(xb)
-        loss = loss_fn(out, lb)
+        loss = model_loss(model, xb, lb)
         loss.backward()
         finish_allreduce(ar, params, ws)
         opt.step()
@@ -520,7 +525,7 @@ def main():
 
         def step_s(xb, lb):
             opt_s.zero_grad(set_to_none=True)
-            loss = loss_fn(model_s(xb), lb)
+            loss = model_loss(model_s, xb, lb)
             loss.backward()
             finish_allreduce(ar_s, params_s, ws)
             opt_s.step()

@@ -257,6 +257,18 @@ int delrec_linear_backward(int M, int K, int N, const float* x, const float* W, 
                            int x_binary, float* dx, float* dW, float* dbias, void* workspace,
                            size_t workspace_bytes, void* stream);
 
+/* ---- readout + time sum of the loss ----------------------------------------------- */
+/* The model zoo's readout Linear (networks.py:140-181) followed by the SSC / PS-MNIST
+ * loss's sum over time (utils.py:188-200, calc_loss_SSC), fused: out (B,C) =
+ * sum_t (y_t W^T + bias) = ysum W^T + T bias with ysum (B,N) = sum_t y_t written too; the
+ * (T,B,C) readout is never formed.  y (T,B,N), W (C,N) as torch.nn.Linear, bias (C) or
+ * NULL.  Backward with g (B,C) = dloss/dout: dy (T,B,N) = g W for every t, dW (C,N) =
+ * g^T ysum, dbias (C) = T sum_b g (any output may be NULL).  fp32, fixed summation order. */
+int delrec_readout_sum_forward(int T, int B, int N, int C, const float* y, const float* W,
+                               const float* bias, float* ysum, float* out, void* stream);
+int delrec_readout_sum_backward(int T, int B, int N, int C, const float* ysum, const float* W,
+                                const float* g, float* dy, float* dW, float* dbias, void* stream);
+
 /* Sets *count (device) to the number of entries of x[0..n) that are neither 0 nor 1;
  * asynchronous on the stream, x 16-byte aligned.  The projections' spike-input test
  * (x_binary above); no counterpart in the reference, whose projections are fp32 GEMMs. */

@@ -23,6 +23,7 @@
 #include "linear.cuh"
 #include "misc.cuh"
 #include "prep.cuh"
+#include "readout.cuh"
 
 namespace delrec {
 
@@ -1714,6 +1715,36 @@ int delrec_hybrid_backward(const delrec_layer* ly, const delrec_lif* lif, const 
                            const float* s, const float* keep, const delrec_grads* g, void* ws, size_t wsb,
                            void* stream) {
   return run_backward(ly, DELREC_HYBRID, lif, gy, u, y, W, base, offsets, s, keep, g, ws, wsb, (cudaStream_t)stream);
+}
+
+int delrec_readout_sum_forward(int T, int B, int N, int C, const float* y, const float* W, const float* bias,
+                               float* ysum, float* out, void* stream) {
+  if (T < 1 || B < 1 || N < 1 || C < 1 || !y || !W || !ysum || !out) return DELREC_ERR_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t BN = (size_t)B * N;
+  k_time_sum<<<grid_for(BN, 256), 256, 0, st>>>(T, BN, y, ysum);
+  DR_LAUNCHED();
+  const size_t warps = (size_t)B * C;
+  k_readout_sum<<<(int)std::min<size_t>((warps + 7) / 8, (size_t)kSMs * 16), 256, 0, st>>>(T, B, N, C, ysum, W,
+                                                                                              bias, out);
+  DR_LAUNCHED();
+  return DELREC_OK;
+}
+
+int delrec_readout_sum_backward(int T, int B, int N, int C, const float* ysum, const float* W, const float* g,
+                                float* dy, float* dW, float* dbias, void* stream) {
+  if (T < 1 || B < 1 || N < 1 || C < 1 || !g || (dy && !W) || (dW && !ysum)) return DELREC_ERR_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t BN = (size_t)B * N, CN = (size_t)C * N;
+  if (dy) {
+    k_readout_sum_dy<<<grid_for(BN, 256), 256, 0, st>>>(T, B, N, C, g, W, dy);
+    DR_LAUNCHED();
+  }
+  if (dW || dbias) {
+    k_readout_sum_dw<<<grid_for(CN + C, 256), 256, 0, st>>>(T, B, N, C, g, ysum, dW, dbias);
+    DR_LAUNCHED();
+  }
+  return DELREC_OK;
 }
 
 int delrec_count_nonbinary(const float* x, size_t n, unsigned int* count, void* stream) {

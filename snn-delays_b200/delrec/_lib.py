@@ -87,6 +87,8 @@ _SIGS = {
     "delrec_scan_time": (_I, [_P, _P]),
     "delrec_scan_time_part": (_I, [_I, _P, _P]),
     "delrec_set_reverse_scan": (_I, [_I]),
+    "delrec_readout_sum_forward": (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
+    "delrec_readout_sum_backward": (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),
     "delrec_exchange_floor_workspace": (_S, [_P]),
     "delrec_exchange_floor": (_I, [_P, _P, _S, _P]),
 }

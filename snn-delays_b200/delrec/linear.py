@@ -83,6 +83,55 @@ class LinearFn(torch.autograd.Function):
         return (dx.view(ctx.xshape) if dx is not None else None), dw, db, None
 
 
+class ReadoutTimeSum(torch.autograd.Function):
+    """sum_t (y_t W^T + bias): the readout Linear of the model zoo (networks.py:140-181)
+    summed over time as the SSC / PS-MNIST loss does (utils.py:188-200), fused in the
+    library (delrec_readout_sum_forward / _backward) without forming the (T,B,C) readout.
+    y (T,B,N), weight (C,N), bias (C) or None -> (B,C)."""
+
+    @staticmethod
+    def forward(ctx, y, weight, bias):
+        _lib.require_cuda(y, weight, bias)
+        T, B, N = y.shape
+        C = weight.shape[0]
+        y = y.detach().contiguous()
+        w = weight.detach().contiguous()
+        b = bias.detach().contiguous() if bias is not None else None
+        ysum = torch.empty(B, N, device=y.device, dtype=torch.float32)
+        out = torch.empty(B, C, device=y.device, dtype=torch.float32)
+        P = _lib.ptr
+        _lib.check(_lib.lib().delrec_readout_sum_forward(T, B, N, C, P(y), P(w), P(b), P(ysum), P(out),
+                                                         _lib.stream_ptr(y.device)),
+                   "delrec_readout_sum_forward")
+        ctx.save_for_backward(ysum, w)
+        ctx.T = T
+        ctx.has_bias = bias is not None
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        ysum, w = ctx.saved_tensors
+        T = ctx.T
+        B, N = ysum.shape
+        C = w.shape[0]
+        g = g.detach().contiguous()
+        dev = g.device
+        dy = torch.empty(T, B, N, device=dev, dtype=torch.float32) if ctx.needs_input_grad[0] else None
+        dW = torch.empty(C, N, device=dev, dtype=torch.float32) if ctx.needs_input_grad[1] else None
+        db = (torch.empty(C, device=dev, dtype=torch.float32)
+              if ctx.has_bias and ctx.needs_input_grad[2] else None)
+        P = _lib.ptr
+        _lib.check(_lib.lib().delrec_readout_sum_backward(T, B, N, C, P(ysum), P(w), P(g), P(dy), P(dW), P(db),
+                                                          _lib.stream_ptr(dev)),
+                   "delrec_readout_sum_backward")
+        return dy, dW, db
+
+
+def readout_time_sum(y, weight, bias=None):
+    """sum over time of the readout y_t W^T + bias, fused (see ReadoutTimeSum)."""
+    return ReadoutTimeSum.apply(y, weight, bias)
+
+
 class Linear(torch.nn.Linear):
     """torch.nn.Linear with the tensor-core fp32-accurate projection of this library."""
 

@@ -18,7 +18,7 @@ import torch
 
 from .dcls import Dcls1d
 from .delay_layers import axonal_recdel, common_recdel, synaptic_recdel
-from .linear import Linear
+from .linear import Linear, readout_time_sum
 from .neuron import BatchNorm1d, Dropout
 
 
@@ -109,6 +109,20 @@ class SNN(torch.nn.Module):
     def forward(self, x):
         assert x.dim() == 3
         return self.layers(x)
+
+    def forward_time_summed(self, x):
+        """sum_t forward(x)[t], (B, output_size): what the SSC / PS-MNIST loss feeds to the
+        cross-entropy (utils.py:188-200, calc_loss_SSC).  With a Linear readout the
+        projection and the time sum run fused in the library, and the (T,B,C) readout is
+        never formed; with a DCLS readout it is forward(x).sum(0)."""
+        assert x.dim() == 3
+        last = self.layers[-1]
+        if type(last) is not Linear:
+            return self.forward(x).sum(0)
+        h = x
+        for m in self.layers[:-1]:
+            h = m(h)
+        return readout_time_sum(h, last.weight, last.bias)
 
     def init_weights(self):
         for m in self.layers:

@@ -98,3 +98,55 @@ def test_spike_input_check():
     assert _is_binary(z[1:])
     z[500] = 2.0
     assert not _is_binary(z[1:])
+
+
+@pytest.mark.parametrize("T,B,N,C,bias", [(32, 64, 64, 4, True), (250, 20, 512, 35, False),
+                                          (7, 3, 33, 10, True)])
+def test_readout_time_sum_matches_fp64(T, B, N, C, bias):
+    """The fused readout + time sum (delrec_readout_sum_forward / _backward): out, dy, dW and
+    dbias against sum_t (y_t W^T + bias) in float64 through autograd."""
+    from delrec.linear import readout_time_sum
+    g = torch.Generator().manual_seed(T + N + C)
+    y = (torch.rand(T, B, N, generator=g) < 0.1).float().cuda().requires_grad_(True)
+    W = (torch.randn(C, N, generator=g) * 0.1).cuda().requires_grad_(True)
+    b = torch.randn(C, generator=g).cuda().requires_grad_(True) if bias else None
+    go = torch.randn(B, C, generator=g).cuda()
+    out = readout_time_sum(y, W, b)
+    (out * go).sum().backward()
+    y64 = y.detach().double().requires_grad_(True)
+    W64 = W.detach().double().requires_grad_(True)
+    b64 = b.detach().double().requires_grad_(True) if bias else None
+    ref = (y64 @ W64.t() + (b64 if bias else 0.0)).sum(0)
+    (ref * go.double()).sum().backward()
+    _close(out, ref.detach(), "out")
+    _close(y.grad, y64.grad, "dy")
+    _close(W.grad, W64.grad, "dW")
+    if bias:
+        _close(b.grad, b64.grad, "dbias")
+
+
+def test_forward_time_summed_matches_the_unfused_model():
+    """A hybrid-delay model's fused readout path (forward_time_summed) against forward()
+    summed over time: the same loss and the same parameter gradients."""
+    from delrec import networks
+    from model_configs import mem_config
+    cfg = mem_config(hidden=(64, 48), bias=True, T=40, B=32)
+    cfg.hybrid_offset_scale = 3
+    torch.manual_seed(0)
+    model = networks.SNN_recurrent_hybrid_delays(cfg).cuda()
+    g = torch.Generator().manual_seed(5)
+    x = (torch.rand(40, 32, cfg.input_size, generator=g) < 0.2).float().cuda()
+    labels = torch.randint(cfg.output_size, (32,), generator=g).cuda()
+    grads = []
+    for fused in (True, False):
+        model.zero_grad(set_to_none=True)
+        out = model.forward_time_summed(x) if fused else model(x).sum(0)
+        loss = torch.nn.functional.cross_entropy(out, labels)
+        loss.backward()
+        grads.append((out.detach(), [p.grad.detach().clone() for p in model.parameters() if p.grad is not None]))
+    (oa, ga), (ob, gb) = grads
+    _close(oa, ob.double(), "out")
+    assert len(ga) == len(gb)
+    for a, b in zip(ga, gb):
+        scale = b.abs().max().item() + 1e-30
+        assert (a - b).abs().max().item() / scale < 1e-4
