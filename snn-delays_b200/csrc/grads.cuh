@@ -224,19 +224,32 @@ __global__ void __launch_bounds__(256, 2) k_source_pass(SrcArgs a, int want_z, i
         h0 = (h0 << 1) | (yw[q] != 0.f ? 1ull : 0ull);
       }
     }
-    // outputs te in [c0, c1), inputs t_in = te + MM
+    // outputs te in [c0, c1), inputs t_in = te + MM; the loads of batch k+1 are issued
+    // before batch k is processed (two batches in flight per thread)
     constexpr int U = 8;
+    float ng[U], nyv[U], ngzv[U][MMX + 1];
+    auto load_batch = [&](int t0) {
+#pragma unroll
+      for (int q = 0; q < U; ++q) {
+        const int te = t0 + q, tin = te + MM;
+        ng[q] = te < c1 ? __ldcs(a.gr + (size_t)te * step + base) : 0.f;
+        nyv[q] = (te < c1 && tin < T) ? __ldcs(a.y + (size_t)tin * step + base) : 0.f;
+#pragma unroll
+        for (int m = 0; m <= MMX; ++m)
+          ngzv[q][m] = (a.gz && m <= MM && te < c1) ? __ldcs(a.gz + (size_t)m * TBN + (size_t)te * step + base) : 0.f;
+      }
+    };
+    load_batch(c0);
     for (int t0 = c0; t0 < c1; t0 += U) {
       float g[U], yv[U], gzv[U][MMX + 1];
 #pragma unroll
       for (int q = 0; q < U; ++q) {
-        const int te = t0 + q, tin = te + MM;
-        g[q] = te < c1 ? __ldcs(a.gr + (size_t)te * step + base) : 0.f;
-        yv[q] = (te < c1 && tin < T) ? __ldcs(a.y + (size_t)tin * step + base) : 0.f;
+        g[q] = ng[q];
+        yv[q] = nyv[q];
 #pragma unroll
-        for (int m = 0; m <= MMX; ++m)
-          gzv[q][m] = (a.gz && m <= MM && te < c1) ? __ldcs(a.gz + (size_t)m * TBN + (size_t)te * step + base) : 0.f;
+        for (int m = 0; m <= MMX; ++m) gzv[q][m] = ngzv[q][m];
       }
+      if (t0 + U < c1) load_batch(t0 + U);
 #pragma unroll
       for (int q = 0; q < U; ++q) {
         const int te = t0 + q;
