@@ -1316,6 +1316,8 @@ static int run_backward(const delrec_layer* ly, int kind, const delrec_lif* lif,
   const size_t TBN = (size_t)T * B * N;
   Carve c(ws, wsb);
   float* gr = c.take<float>(TBN);
+  // without dropout gr = du * 1 = dx: the scans' gr is dx itself (one array written once)
+  if (!ly->has_keep) gr = g->dx;
   float *gz = nullptr, *tw = nullptr;
   int *tl0 = nullptr, *tnt = nullptr;
   if (kind != DELREC_SYNAPTIC) {

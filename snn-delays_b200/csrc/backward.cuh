@@ -166,7 +166,7 @@ __global__ void __launch_bounds__(256) k_bwd(BwdArgs a) {
         const float kp = a.keep ? a.keep[(size_t)b * N + o] : 1.f;
         grv = __fmul_rn(du, kp);
         a.dx[idx] = du;
-        a.gr[idx] = grv;
+        if (a.gr != a.dx) a.gr[idx] = grv;   // (gr is dx itself without dropout)
       }
       if (ol < nts) grc[(size_t)(o0 + ol) * BT + bl] = grv;
     }

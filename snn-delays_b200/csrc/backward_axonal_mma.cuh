@@ -368,7 +368,7 @@ __global__ void __launch_bounds__(512, 1) k_bwd_axonal_mma(AxMmaArgs a) {
         grv = __fmul_rn(du, kp[k]);
         const size_t idx = ((size_t)t * B + b0 + bl) * N + o0 + ol;
         a.dx[idx] = du;
-        a.gr[idx] = grv;
+        if (a.gr != a.dx) a.gr[idx] = grv;   // (gr is dx itself without dropout)
       }
       rrow[((t + 2) % KMAX) * 64] = 0.f;   // last read of slot t+2 was above
       __stcg(xb + (size_t)bl * N + o0 + ol, grv);

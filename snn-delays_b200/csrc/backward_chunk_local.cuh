@@ -340,7 +340,7 @@ __global__ void __launch_bounds__(NTH, 1) k_bwd_chunk_local(LocArgs la) {
         const int b = b0 + bl;
         const size_t idx = ((size_t)t * B + b) * N + o;
         a.dx[idx] = du;
-        a.gr[idx] = grv;
+        if (a.gr != a.dx) a.gr[idx] = grv;   // (gr is dx itself without dropout)
         const __nv_bfloat16 h = __float2bfloat16_rn(grv);
         const size_t ai = ((size_t)b * T + t) * a.Np + o;
         a.ga_hi[ai] = h;

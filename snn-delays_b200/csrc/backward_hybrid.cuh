@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid(HybArgs a) {
         const float kp = a.keep ? a.keep[(size_t)b * N + o] : 1.f;
         grv = __fmul_rn(du, kp);
         a.dx[idx] = du;
-        a.gr[idx] = grv;
+        if (a.gr != a.dx) a.gr[idx] = grv;   // (gr is dx itself without dropout)
       }
       if (bl < BT && ol < nts) grc[(size_t)(o0 + ol) * BT + bl] = grv;
     }

@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(512, 1) k_bwd_hybrid64(Hyb64Args a) {
         grv = __fmul_rn(du, kp[k]);
         const size_t idx = ((size_t)t * B + b0 + bl) * N + o0 + ol;
         a.dx[idx] = du;
-        a.gr[idx] = grv;
+        if (a.gr != a.dx) a.gr[idx] = grv;   // (gr is dx itself without dropout)
       }
       // slot t+2 (== t-K mod KMAX) had its last read above; it next receives gz(t-K)
       rrow[((t + 2) % KMAX) * 64] = 0.f;
