@@ -143,12 +143,36 @@ __global__ void __launch_bounds__(kLocThreads, 1)
   }
   if (tid == 0) s_cum[min(N, 1024)] = carry;
   __syncthreads();
-  // one warp per source copies its cached prefix
-  for (int o = warp; o < N; o += kLocThreads / 32) {
-    const int at = s_cum[o], len = s_cum[o + 1] - at;
-    for (int pos = lane; pos < len; pos += 32) {
-      cidx[at + pos] = sidx[(size_t)o * CAP + pos];
-      cw[at + pos] = sw[(size_t)o * CAP + pos];
+  // the cached prefixes, copied as one flat range: entry e belongs to the last source o
+  // with s_cum[o] <= e; eight independent loads in flight per thread, coalesced over e
+  {
+    const int Nc = min(N, 1024);
+    for (int e0 = 0; e0 < carry; e0 += 8 * kLocThreads) {
+      uint16_t iv[8];
+      float wv[8];
+      int ev[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int e = e0 + j * kLocThreads + tid;
+        ev[j] = e;
+        if (e < carry) {
+          int lo = 0, hi = Nc;   // s_cum[lo] <= e < s_cum[hi]
+          while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (s_cum[mid] <= e) lo = mid;
+            else hi = mid;
+          }
+          const size_t src = (size_t)lo * CAP + (e - s_cum[lo]);
+          iv[j] = sidx[src];
+          wv[j] = sw[src];
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (ev[j] < carry) {
+          cidx[ev[j]] = iv[j];
+          cw[ev[j]] = wv[j];
+        }
     }
   }
   if (tid == 0) {
