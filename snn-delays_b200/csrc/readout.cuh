@@ -71,7 +71,18 @@ __global__ void k_readout_sum_dw(int T, int B, int N, int C, const float* __rest
       if (!dW) continue;
       const int c = (int)(e / N), n = (int)(e % N);
       float s = 0.f;
-      for (int b = 0; b < B; ++b) s = fmaf(g[(size_t)b * C + c], ysum[(size_t)b * N + n], s);
+      int b = 0;
+      for (; b + 8 <= B; b += 8) {   // eight loads of each operand in flight, summed in order
+        float gv[8], yv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          gv[j] = g[(size_t)(b + j) * C + c];
+          yv[j] = ysum[(size_t)(b + j) * N + n];
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s = fmaf(gv[j], yv[j], s);
+      }
+      for (; b < B; ++b) s = fmaf(g[(size_t)b * C + c], ysum[(size_t)b * N + n], s);
       dW[e] = s;
     } else if (dbias) {
       const int c = (int)(e - CN);
