@@ -1080,16 +1080,33 @@ static size_t chunk_ws(const delrec_layer* ly, const ChunkPlan& cp) {
   return c.off;
 }
 
-// (B, T, N) bf16 pieces read as boxes of 64 targets x 8 steps x 16 samples
+// (B, T, N) bf16 pieces read as boxes of 32 targets x 8 steps x 16 samples (64-byte swizzle)
 static bool tmap_bf16_btn(CUtensorMap* m, const void* base, int N, int T, int B, int Np) {
   TmapEncodeFn fn = tmap_encoder();
   if (!fn || !base || ((uintptr_t)base & 15) || (Np % 8)) return false;
   const cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)T, (cuuint64_t)B};
   const cuuint64_t strides[2] = {(cuuint64_t)Np * 2, (cuuint64_t)T * Np * 2};
-  const cuuint32_t box[3] = {64, (cuuint32_t)kChunk, (cuuint32_t)kGzSamples};
+  const cuuint32_t box[3] = {(cuuint32_t)kGzK, (cuuint32_t)kChunk, (cuuint32_t)kGzSamples};
   const cuuint32_t es[3] = {1, 1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// A bf16 matrix of `rows` x `cols` (row stride ld elements) read as 32-column x box_rows
+// boxes with the 64-byte swizzle (the chunk GEMM's B operand)
+static bool tmap_bf16_k32(CUtensorMap* m, const void* base, long long cols, long long rows, long long ld,
+                          int box_rows) {
+  TmapEncodeFn fn = tmap_encoder();
+  if (!fn || !base || cols < 1 || rows < 1 || box_rows < 8 || box_rows > 256 || ((uintptr_t)base & 15) ||
+      ((ld * 2) & 15) || ld < cols)
+    return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  const cuuint32_t box[2] = {(cuuint32_t)kGzK, (cuuint32_t)box_rows};
+  const cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -1103,7 +1120,7 @@ static int launch_gz_t(const CUtensorMap* m, const GzArgs& g, int ntiles, cudaSt
   const int total = cdiv(g.B, kGzSamples) * ntiles;
   cudaLaunchAttribute attr[1];
   const cudaLaunchConfig_t cfg = pdl_config(dim3(std::min(total, kSMs)), dim3(kGzThreads), kGzSmem, st, pdl, attr);
-  DR_CUDA(cudaLaunchKernelEx(&cfg, kern, m[0], m[1], m[2], m[3], ga));
+  DR_CUDA(cudaLaunchKernelEx(&cfg, kern, m[0], m[1], m[2], m[3], m[4], m[5], ga));
   DR_LAUNCHED();
   return DELREC_OK;
 }
@@ -1147,10 +1164,14 @@ static int run_chunked(const delrec_layer* ly, const Hyb64Plan& h64, const Chunk
   k_mask_w<<<grid_for(wrows * Np, 256), 256, 0, st>>>(N, Np, cp.KP1, (int)wrows, W, offT, wm_hi, wm_lo);
   DR_LAUNCHED();
   DR_CUDA(cudaMemsetAsync(gz, 0, (size_t)T * B * N * sizeof(float), st));
-  CUtensorMap maps[4];
+  // the last column tile's sources, and its MMA width (used columns rounded up to 16)
+  const int ncl = std::min(kGzCols, ((N - (cp.ntiles - 1) * gz_ntg(cp.KP1)) * cp.KP1 + 15) & ~15);
+  CUtensorMap maps[6];
   if (!tmap_bf16_btn(&maps[0], ga_hi, N, T, B, Np) || !tmap_bf16_btn(&maps[1], ga_lo, N, T, B, Np) ||
-      !tmap_bf16(&maps[2], wm_hi, N, (long long)wrows, Np, kGzCols) ||
-      !tmap_bf16(&maps[3], wm_lo, N, (long long)wrows, Np, kGzCols))
+      !tmap_bf16_k32(&maps[2], wm_hi, N, (long long)wrows, Np, kGzCols) ||
+      !tmap_bf16_k32(&maps[3], wm_lo, N, (long long)wrows, Np, kGzCols) ||
+      !tmap_bf16_k32(&maps[4], wm_hi, N, (long long)wrows, Np, ncl) ||
+      !tmap_bf16_k32(&maps[5], wm_lo, N, (long long)wrows, Np, ncl))
     return DELREC_ERR_ARG;
   // steps: the sample-local kernel (no exchange) unless the exchange form is selected
   const bool local = g_reverse_scan.load() != 2 || !cp.exch;
@@ -1192,7 +1213,7 @@ static int run_chunked(const delrec_layer* ly, const Hyb64Plan& h64, const Chunk
   a.dx = base.dx; a.gr = base.gr; a.gz = gz; a.ga_hi = ga_hi; a.ga_lo = ga_lo; a.Np = Np; a.lam = lam;
   a.lif = base.lif; a.grx = base.grx; a.arrive = base.arrive; a.spin_limit = base.spin_limit;
   GzArgs g{};
-  g.T = T; g.B = B; g.N = N; g.gz = gz; g.spin_ns = 2000000000ll;
+  g.T = T; g.B = B; g.N = N; g.ncl = ncl; g.gz = gz; g.spin_ns = 2000000000ll;
   if (!local) DR_CUDA(cudaMemsetAsync(a.arrive, 0, sizeof(unsigned int) * h64.tiles, st));
   scan_mark(0, st);
   for (int ch = cp.nchunks - 1; ch >= 0; --ch) {

@@ -353,21 +353,38 @@ __global__ void __launch_bounds__(512, 1) k_exchange_floor(int T, int N, int CS,
 }
 
 // ---- the chunk GEMM ---------------------------------------------------------------------
-constexpr int kGzRows = 128, kGzCols = 256, kGzSamples = kGzRows / kChunk, kGzStages = 2;
+// Reduction blocks of 32 (64-byte rows, 64-byte swizzle) in a four-stage ring: a stage is
+// 48 KB (both pieces of A and B), so three stages are in flight while the MMAs read one.
+constexpr int kGzRows = 128, kGzCols = 256, kGzSamples = kGzRows / kChunk, kGzK = 32, kGzStages = 4;
 // sources per column tile: as many as 256 columns hold, rounded down to a multiple of 4 (the
 // epilogue adds groups of 4 consecutive sources with one vector reduction)
 __host__ __device__ constexpr int gz_ntg(int KP1) { return (kGzCols / KP1) & ~3; }
-constexpr uint32_t kGzABytes = kGzRows * 64 * 2, kGzBBytes = kGzCols * 64 * 2;
+constexpr uint32_t kGzABytes = kGzRows * kGzK * 2, kGzBBytes = kGzCols * kGzK * 2;
 constexpr uint32_t kGzStageBytes = 2 * kGzABytes + 2 * kGzBBytes;
 constexpr size_t kGzSmem = (size_t)kGzStages * kGzStageBytes + 1024;
 
 constexpr int kGzEpiWarps = 4, kGzThreads = 64 + 32 * kGzEpiWarps;
 
+// The last column tile holds the sources left over (N - (ntiles-1) * gz_ntg); its MMAs
+// are `ncl` columns wide (the used columns rounded up to 16) and its B boxes `ncl` rows.
 struct GzArgs {
-  int T, B, N, t0, ntiles;
+  int T, B, N, t0, ntiles, ncl;
   float* gz;
   long long spin_ns;
 };
+
+// Shared-memory descriptor of a K-major tile written by TMA with the 64-byte swizzle (tile
+// base 512-aligned): rows of 64 bytes (32 reduction elements), 8-row groups 512 bytes
+// apart; the next K=16 slice starts 32 bytes further.
+__device__ __forceinline__ uint64_t umma_desc_sw64(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);   // start address
+  d |= (uint64_t)1 << 16;                      // leading byte offset (unused when swizzled)
+  d |= (uint64_t)(512 >> 4) << 32;             // stride byte offset
+  d |= (uint64_t)1 << 46;                      // descriptor version
+  d |= (uint64_t)4 << 61;                      // 64-byte swizzle
+  return d;
+}
 
 // gz[0..3] += v (one vector reduction; gz 16-byte aligned)
 __device__ __forceinline__ void red_add_v4(float* gz, float a, float b, float c, float d) {
@@ -386,10 +403,11 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
 // so the CTAs of a wave share the masked-W tile of their column block through L2).
 // A tile is 16 samples x the chunk's 8 steps (rows b*8 + q) against 256 (source, offset)
 // columns (source-major, KP1 = K+1 offsets per source, gz_ntg(KP1) sources per tile);
-// A = gr pieces from the (B, T, Np) layout through a 3-D tensor map (box 64 x 8 x 16),
-// B = the offset-masked W pieces (tile rows of 256, K-major).
-// Warp roles: warp 0 streams the four pieces of each 64-wide reduction block through a
-// two-stage ring (TMA, per-CTA loads); warp 1 issues 12 MMAs per block (3 products x 4
+// A = gr pieces from the (B, T, Np) layout through a 3-D tensor map (box 32 x 8 x 16),
+// B = the offset-masked W pieces (tile rows of 256, K-major; the last column tile's maps
+// have boxes of ncl rows).
+// Warp roles: warp 0 streams the four pieces of each 32-wide reduction block through a
+// four-stage ring (TMA, per-CTA loads); warp 1 issues 6 MMAs per block (3 products x 2
 // K-steps) into one of two tensor-memory accumulators (256 columns each), so the MMAs of
 // the next tile run while warps 2..5 drain the previous one; the epilogue warps read their
 // 32-lane quarter of the accumulator (thread = row (b, q)), form the shift sums over the
@@ -397,7 +415,8 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
 template <int KP1>
 __global__ void __launch_bounds__(kGzThreads, 1)
     k_chunk_gz(const __grid_constant__ CUtensorMap mahi, const __grid_constant__ CUtensorMap malo,
-               const __grid_constant__ CUtensorMap mbhi, const __grid_constant__ CUtensorMap mblo, const GzArgs g) {
+               const __grid_constant__ CUtensorMap mbhi, const __grid_constant__ CUtensorMap mblo,
+               const __grid_constant__ CUtensorMap mlhi, const __grid_constant__ CUtensorMap mllo, const GzArgs g) {
   static_assert(KP1 >= 1 && KP1 <= kChunk + 1, "offset window wider than two chunks");
   constexpr int NTG = gz_ntg(KP1), USED = NTG * KP1;
   extern __shared__ unsigned char dsm[];
@@ -408,8 +427,9 @@ __global__ void __launch_bounds__(kGzThreads, 1)
   const uint32_t base = (smem_u32(dsm) + 1023u) & ~1023u;
   const uint32_t full0 = smem_u32(&bars[0]), empty0 = smem_u32(&bars[kGzStages]);
   const uint32_t accf0 = smem_u32(&bars[2 * kGzStages]), acce0 = smem_u32(&bars[2 * kGzStages + 2]);
-  const int t0 = g.t0, kb = (g.N + 63) / 64;
+  const int t0 = g.t0, kb = (g.N + kGzK - 1) / kGzK;
   const int tiles_m = (g.B + kGzSamples - 1) / kGzSamples, total = tiles_m * g.ntiles;
+  const int last_n = g.ntiles - 1;
 
   if (tid == 0) {
     for (int s = 0; s < kGzStages; ++s) {
@@ -424,6 +444,7 @@ __global__ void __launch_bounds__(kGzThreads, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&mahi) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&mbhi) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"((unsigned long long)&mlhi) : "memory");
   }
   if (warp == 2) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
@@ -446,25 +467,31 @@ __global__ void __launch_bounds__(kGzThreads, 1)
     if (lane == 0) {
       int it = 0;
       for (int tile = blockIdx.x; tile < total && !*abort; tile += gridDim.x) {
-        const int b0 = (tile % tiles_m) * kGzSamples, n0 = (tile / tiles_m) * kGzCols;
+        const int b0 = (tile % tiles_m) * kGzSamples, n = tile / tiles_m, n0 = n * kGzCols;
+        const bool narrow = n == last_n;
+        const CUtensorMap* bh = narrow ? &mlhi : &mbhi;
+        const CUtensorMap* bl = narrow ? &mllo : &mblo;
+        const uint32_t bbytes = narrow ? (uint32_t)g.ncl * kGzK * 2 : kGzBBytes;
         for (int j = 0; j < kb; ++j, ++it) {
           const int s = it % kGzStages;
           const uint32_t ph = (uint32_t)(it / kGzStages) & 1u;
           if (!mbar_wait(empty0 + 8 * s, ph ^ 1u, g.spin_ns, abort)) break;
           const uint32_t st = base + s * kGzStageBytes;
-          mbar_expect_tx(full0 + 8 * s, kGzStageBytes);
-          tma_load_3d(st, &mahi, j * 64, t0, b0, full0 + 8 * s);
-          tma_load_3d(st + kGzABytes, &malo, j * 64, t0, b0, full0 + 8 * s);
-          tma_load_2d(st + 2 * kGzABytes, &mbhi, j * 64, n0, full0 + 8 * s);
-          tma_load_2d(st + 2 * kGzABytes + kGzBBytes, &mblo, j * 64, n0, full0 + 8 * s);
+          mbar_expect_tx(full0 + 8 * s, 2 * kGzABytes + 2 * bbytes);
+          tma_load_3d(st, &mahi, j * kGzK, t0, b0, full0 + 8 * s);
+          tma_load_3d(st + kGzABytes, &malo, j * kGzK, t0, b0, full0 + 8 * s);
+          tma_load_2d(st + 2 * kGzABytes, bh, j * kGzK, n0, full0 + 8 * s);
+          tma_load_2d(st + 2 * kGzABytes + kGzBBytes, bl, j * kGzK, n0, full0 + 8 * s);
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(kGzCols, false, false);
+      constexpr uint32_t idesc_full = umma_idesc_bf16(kGzCols, false, false);
+      const uint32_t idesc_narrow = (idesc_full & ~(0x3Fu << 17)) | ((uint32_t)(g.ncl >> 3) << 17);
       int it = 0, lt = 0;
       for (int tile = blockIdx.x; tile < total && !*abort; tile += gridDim.x, ++lt) {
+        const uint32_t idesc = tile / tiles_m == last_n ? idesc_narrow : idesc_full;
         const int acc = lt & 1;
         const uint32_t u = (uint32_t)(lt >> 1);
         // the epilogue has drained this accumulator's previous tile
@@ -478,11 +505,11 @@ __global__ void __launch_bounds__(kGzThreads, 1)
           if (!mbar_wait(full0 + 8 * s, ph, g.spin_ns, abort)) { ok = false; break; }
           tc_fence_after();
           const uint32_t st = base + s * kGzStageBytes;
-          const uint64_t ahi = umma_desc_sw128(st, false), alo = umma_desc_sw128(st + kGzABytes, false);
-          const uint64_t bhi = umma_desc_sw128(st + 2 * kGzABytes, false);
-          const uint64_t blo = umma_desc_sw128(st + 2 * kGzABytes + kGzBBytes, false);
+          const uint64_t ahi = umma_desc_sw64(st), alo = umma_desc_sw64(st + kGzABytes);
+          const uint64_t bhi = umma_desc_sw64(st + 2 * kGzABytes);
+          const uint64_t blo = umma_desc_sw64(st + 2 * kGzABytes + kGzBBytes);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
+          for (int kk = 0; kk < kGzK / 16; ++kk) {
             umma_bf16(d, ahi + 2 * kk, bhi + 2 * kk, idesc, (j > 0 || kk > 0) ? 1u : 0u);
             umma_bf16(d, ahi + 2 * kk, blo + 2 * kk, idesc, 1u);
             umma_bf16(d, alo + 2 * kk, bhi + 2 * kk, idesc, 1u);
@@ -505,6 +532,9 @@ __global__ void __launch_bounds__(kGzThreads, 1)
       const int acc = lt & 1;
       const uint32_t u = (uint32_t)(lt >> 1);
       const int b0 = (tile % tiles_m) * kGzSamples, ob = (tile / tiles_m) * NTG;
+      // columns the MMAs wrote (the narrow tile's columns past ncl hold an older tile's
+      // values; they belong to sources >= N, whose sums are never added)
+      const int wcols = tile / tiles_m == last_n ? g.ncl : kGzCols;
       const bool ok = __all_sync(0xffffffffu, mbar_wait(accf0 + 8 * acc, u & 1u, g.spin_ns, abort));
       if (!ok) break;
       tc_fence_after();
@@ -517,7 +547,7 @@ __global__ void __launch_bounds__(kGzThreads, 1)
       for (int i = 0; i < 4; ++i) a0[i] = a1[i] = 0.f;
 #pragma unroll
       for (int cc = 0; cc < kGzCols / 32; ++cc) {
-        if (cc * 32 >= USED) break;
+        if (cc * 32 >= USED || cc * 32 >= wcols) break;
         float v[32];
         tmem_ld32(tmem + ((uint32_t)(qd * 32) << 16) + (uint32_t)(acc * kGzCols + cc * 32), v);
 #pragma unroll
