@@ -1117,7 +1117,7 @@ static int launch_gz_t(const CUtensorMap* m, const GzArgs& g, int ntiles, cudaSt
   if (rc) return rc;
   GzArgs ga = g;
   ga.ntiles = ntiles;
-  const int total = cdiv(g.B, kGzSamples) * ntiles;
+  const int total = gz_items(cdiv(g.B, kGzSamples), ntiles, g.ncl);
   cudaLaunchAttribute attr[1];
   const cudaLaunchConfig_t cfg = pdl_config(dim3(std::min(total, kSMs)), dim3(kGzThreads), kGzSmem, st, pdl, attr);
   DR_CUDA(cudaLaunchKernelEx(&cfg, kern, m[0], m[1], m[2], m[3], m[4], m[5], ga));

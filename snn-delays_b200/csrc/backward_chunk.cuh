@@ -373,6 +373,36 @@ struct GzArgs {
   long long spin_ns;
 };
 
+// Work items of one launch: tile n * tiles_m + m of each full column block (n < ntiles-1),
+// then the last column block's sample tiles, two per item (m = 2r, 2r+1) when that block
+// is at most 128 columns wide: both tiles share the item's B stage and one accumulator
+// (columns 0.. and 128..), so a launch has fewer items to spread over the SMs.
+struct GzItem {
+  int n, m;
+  bool two;
+};
+__host__ __device__ inline int gz_items(int tiles_m, int ntiles, int ncl) {
+  return (ntiles - 1) * tiles_m + (ncl <= kGzCols / 2 ? (tiles_m + 1) / 2 : tiles_m);
+}
+__device__ __forceinline__ GzItem gz_item(int it, int tiles_m, int ntiles, int ncl) {
+  const int nfull = (ntiles - 1) * tiles_m;
+  GzItem w;
+  if (it < nfull) {
+    w.n = it / tiles_m;
+    w.m = it % tiles_m;
+    w.two = false;
+  } else if (ncl <= kGzCols / 2) {
+    w.n = ntiles - 1;
+    w.m = 2 * (it - nfull);
+    w.two = w.m + 1 < tiles_m;
+  } else {
+    w.n = ntiles - 1;
+    w.m = it - nfull;
+    w.two = false;
+  }
+  return w;
+}
+
 // Shared-memory descriptor of a K-major tile written by TMA with the 64-byte swizzle (tile
 // base 512-aligned): rows of 64 bytes (32 reduction elements), 8-row groups 512 bytes
 // apart; the next K=16 slice starts 32 bytes further.
@@ -399,8 +429,9 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// Persistent chunk GEMM: one CTA per SM walks the output tiles (tile id = n * tiles_m + m,
-// so the CTAs of a wave share the masked-W tile of their column block through L2).
+// Persistent chunk GEMM: one CTA per SM walks the work items (gz_item: tile n * tiles_m + m
+// of the full column blocks, so the CTAs of a wave share the masked-W tile of their column
+// block through L2; then the last block's tiles, in pairs when it is narrow).
 // A tile is 16 samples x the chunk's 8 steps (rows b*8 + q) against 256 (source, offset)
 // columns (source-major, KP1 = K+1 offsets per source, gz_ntg(KP1) sources per tile);
 // A = gr pieces from the (B, T, Np) layout through a 3-D tensor map (box 32 x 8 x 16),
@@ -428,7 +459,7 @@ __global__ void __launch_bounds__(kGzThreads, 1)
   const uint32_t full0 = smem_u32(&bars[0]), empty0 = smem_u32(&bars[kGzStages]);
   const uint32_t accf0 = smem_u32(&bars[2 * kGzStages]), acce0 = smem_u32(&bars[2 * kGzStages + 2]);
   const int t0 = g.t0, kb = (g.N + kGzK - 1) / kGzK;
-  const int tiles_m = (g.B + kGzSamples - 1) / kGzSamples, total = tiles_m * g.ntiles;
+  const int tiles_m = (g.B + kGzSamples - 1) / kGzSamples, total = gz_items(tiles_m, g.ntiles, g.ncl);
   const int last_n = g.ntiles - 1;
 
   if (tid == 0) {
@@ -466,9 +497,10 @@ __global__ void __launch_bounds__(kGzThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       int it = 0;
-      for (int tile = blockIdx.x; tile < total && !*abort; tile += gridDim.x) {
-        const int b0 = (tile % tiles_m) * kGzSamples, n = tile / tiles_m, n0 = n * kGzCols;
-        const bool narrow = n == last_n;
+      for (int item = blockIdx.x; item < total && !*abort; item += gridDim.x) {
+        const GzItem w = gz_item(item, tiles_m, g.ntiles, g.ncl);
+        const int b0 = w.m * kGzSamples, n0 = w.n * kGzCols;
+        const bool narrow = w.n == last_n;
         const CUtensorMap* bh = narrow ? &mlhi : &mbhi;
         const CUtensorMap* bl = narrow ? &mllo : &mblo;
         const uint32_t bbytes = narrow ? (uint32_t)g.ncl * kGzK * 2 : kGzBBytes;
@@ -476,12 +508,16 @@ __global__ void __launch_bounds__(kGzThreads, 1)
           const int s = it % kGzStages;
           const uint32_t ph = (uint32_t)(it / kGzStages) & 1u;
           if (!mbar_wait(empty0 + 8 * s, ph ^ 1u, g.spin_ns, abort)) break;
-          const uint32_t st = base + s * kGzStageBytes;
-          mbar_expect_tx(full0 + 8 * s, 2 * kGzABytes + 2 * bbytes);
-          tma_load_3d(st, &mahi, j * kGzK, t0, b0, full0 + 8 * s);
-          tma_load_3d(st + kGzABytes, &malo, j * kGzK, t0, b0, full0 + 8 * s);
-          tma_load_2d(st + 2 * kGzABytes, bh, j * kGzK, n0, full0 + 8 * s);
-          tma_load_2d(st + 2 * kGzABytes + kGzBBytes, bl, j * kGzK, n0, full0 + 8 * s);
+          const uint32_t st = base + s * kGzStageBytes, fb = full0 + 8 * s;
+          mbar_expect_tx(fb, (w.two ? 4u : 2u) * kGzABytes + 2u * bbytes);
+          tma_load_3d(st, &mahi, j * kGzK, t0, b0, fb);
+          tma_load_3d(st + kGzABytes, &malo, j * kGzK, t0, b0, fb);
+          tma_load_2d(st + 2 * kGzABytes, bh, j * kGzK, n0, fb);
+          tma_load_2d(st + 2 * kGzABytes + kGzBBytes, bl, j * kGzK, n0, fb);
+          if (w.two) {   // the second tile's A pieces in the upper halves of the B regions
+            tma_load_3d(st + 2 * kGzABytes + kGzBBytes / 2, &mahi, j * kGzK, t0, b0 + kGzSamples, fb);
+            tma_load_3d(st + 2 * kGzABytes + kGzBBytes + kGzBBytes / 2, &malo, j * kGzK, t0, b0 + kGzSamples, fb);
+          }
         }
       }
     }
@@ -490,8 +526,9 @@ __global__ void __launch_bounds__(kGzThreads, 1)
       constexpr uint32_t idesc_full = umma_idesc_bf16(kGzCols, false, false);
       const uint32_t idesc_narrow = (idesc_full & ~(0x3Fu << 17)) | ((uint32_t)(g.ncl >> 3) << 17);
       int it = 0, lt = 0;
-      for (int tile = blockIdx.x; tile < total && !*abort; tile += gridDim.x, ++lt) {
-        const uint32_t idesc = tile / tiles_m == last_n ? idesc_narrow : idesc_full;
+      for (int item = blockIdx.x; item < total && !*abort; item += gridDim.x, ++lt) {
+        const GzItem w = gz_item(item, tiles_m, g.ntiles, g.ncl);
+        const uint32_t idesc = w.n == last_n ? idesc_narrow : idesc_full;
         const int acc = lt & 1;
         const uint32_t u = (uint32_t)(lt >> 1);
         // the epilogue has drained this accumulator's previous tile
@@ -514,6 +551,17 @@ __global__ void __launch_bounds__(kGzThreads, 1)
             umma_bf16(d, ahi + 2 * kk, blo + 2 * kk, idesc, 1u);
             umma_bf16(d, alo + 2 * kk, bhi + 2 * kk, idesc, 1u);
           }
+          if (w.two) {   // second sample tile into accumulator columns 128..
+            const uint64_t a1hi = umma_desc_sw64(st + 2 * kGzABytes + kGzBBytes / 2);
+            const uint64_t a1lo = umma_desc_sw64(st + 2 * kGzABytes + kGzBBytes + kGzBBytes / 2);
+            const uint32_t d1 = d + (uint32_t)(kGzCols / 2);
+#pragma unroll
+            for (int kk = 0; kk < kGzK / 16; ++kk) {
+              umma_bf16(d1, a1hi + 2 * kk, bhi + 2 * kk, idesc, (j > 0 || kk > 0) ? 1u : 0u);
+              umma_bf16(d1, a1hi + 2 * kk, blo + 2 * kk, idesc, 1u);
+              umma_bf16(d1, a1lo + 2 * kk, bhi + 2 * kk, idesc, 1u);
+            }
+          }
           umma_commit(empty0 + 8 * s);
         }
         if (!ok) break;
@@ -528,51 +576,55 @@ __global__ void __launch_bounds__(kGzThreads, 1)
     const bool vec = (g.N & 3) == 0;
     const int s0 = t0 + q, s1 = t0 + q - kChunk;
     int lt = 0;
-    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++lt) {
+    for (int item = blockIdx.x; item < total; item += gridDim.x, ++lt) {
+      const GzItem w = gz_item(item, tiles_m, g.ntiles, g.ncl);
       const int acc = lt & 1;
       const uint32_t u = (uint32_t)(lt >> 1);
-      const int b0 = (tile % tiles_m) * kGzSamples, ob = (tile / tiles_m) * NTG;
+      const int ob = w.n * NTG;
       // columns the MMAs wrote (the narrow tile's columns past ncl hold an older tile's
       // values; they belong to sources >= N, whose sums are never added)
-      const int wcols = tile / tiles_m == last_n ? g.ncl : kGzCols;
+      const int wcols = w.n == last_n ? g.ncl : kGzCols;
       const bool ok = __all_sync(0xffffffffu, mbar_wait(accf0 + 8 * acc, u & 1u, g.spin_ns, abort));
       if (!ok) break;
       tc_fence_after();
-      const int b = b0 + qd * 4 + (lane >> 3);
-      const bool brow = b < g.B;
-      float* row0 = (brow && s0 < g.T) ? g.gz + (size_t)s0 * BN + (size_t)b * g.N : nullptr;
-      float* row1 = (brow && s1 >= 0) ? g.gz + (size_t)s1 * BN + (size_t)b * g.N : nullptr;
-      float a0[4], a1[4];
+      for (int h = 0; h < (w.two ? 2 : 1); ++h) {   // sample tile m + h at accumulator column 128 h
+        const int b = (w.m + h) * kGzSamples + qd * 4 + (lane >> 3);
+        const bool brow = b < g.B;
+        float* row0 = (brow && s0 < g.T) ? g.gz + (size_t)s0 * BN + (size_t)b * g.N : nullptr;
+        float* row1 = (brow && s1 >= 0) ? g.gz + (size_t)s1 * BN + (size_t)b * g.N : nullptr;
+        const uint32_t taddr = tmem + ((uint32_t)(qd * 32) << 16) + (uint32_t)(acc * kGzCols + h * (kGzCols / 2));
+        float a0[4], a1[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) a0[i] = a1[i] = 0.f;
+        for (int i = 0; i < 4; ++i) a0[i] = a1[i] = 0.f;
 #pragma unroll
-      for (int cc = 0; cc < kGzCols / 32; ++cc) {
-        if (cc * 32 >= USED || cc * 32 >= wcols) break;
-        float v[32];
-        tmem_ld32(tmem + ((uint32_t)(qd * 32) << 16) + (uint32_t)(acc * kGzCols + cc * 32), v);
+        for (int cc = 0; cc < kGzCols / 32; ++cc) {
+          if (cc * 32 >= USED || cc * 32 >= wcols) break;
+          float v[32];
+          tmem_ld32(taddr + (uint32_t)(cc * 32), v);
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const int c = cc * 32 + jj;
-          if (c < USED) {
-            const int k = c % KP1, ol = c / KP1, g4 = ol & 3;
-            const int src = q + k;   // lane of row tau = t0 + src (window 0) or t0 + src - 8
-            const float x = __shfl_sync(0xffffffffu, v[jj], grp | (src & 7));
-            if (src < kChunk) a0[g4] += x;
-            else a1[g4] += x;
-            if (k == KP1 - 1 && g4 == 3) {   // sources ol-3 .. ol complete
-              const int o = ob + ol - 3;
-              if (vec) {
-                if (row0 && o < g.N) red_add_v4(row0 + o, a0[0], a0[1], a0[2], a0[3]);
-                if (row1 && o < g.N) red_add_v4(row1 + o, a1[0], a1[1], a1[2], a1[3]);
-              } else {
+          for (int jj = 0; jj < 32; ++jj) {
+            const int c = cc * 32 + jj;
+            if (c < USED) {
+              const int k = c % KP1, ol = c / KP1, g4 = ol & 3;
+              const int src = q + k;   // lane of row tau = t0 + src (window 0) or t0 + src - 8
+              const float x = __shfl_sync(0xffffffffu, v[jj], grp | (src & 7));
+              if (src < kChunk) a0[g4] += x;
+              else a1[g4] += x;
+              if (k == KP1 - 1 && g4 == 3) {   // sources ol-3 .. ol complete
+                const int o = ob + ol - 3;
+                if (vec) {
+                  if (row0 && o < g.N) red_add_v4(row0 + o, a0[0], a0[1], a0[2], a0[3]);
+                  if (row1 && o < g.N) red_add_v4(row1 + o, a1[0], a1[1], a1[2], a1[3]);
+                } else {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  if (row0 && o + i < g.N) atomicAdd(row0 + o + i, a0[i]);
-                  if (row1 && o + i < g.N) atomicAdd(row1 + o + i, a1[i]);
+                  for (int i = 0; i < 4; ++i) {
+                    if (row0 && o + i < g.N) atomicAdd(row0 + o + i, a0[i]);
+                    if (row1 && o + i < g.N) atomicAdd(row1 + o + i, a1[i]);
+                  }
                 }
-              }
 #pragma unroll
-              for (int i = 0; i < 4; ++i) a0[i] = a1[i] = 0.f;
+                for (int i = 0; i < 4; ++i) a0[i] = a1[i] = 0.f;
+              }
             }
           }
         }
