@@ -437,12 +437,13 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
 // A = gr pieces from the (B, T, Np) layout through a 3-D tensor map (box 32 x 8 x 16),
 // B = the offset-masked W pieces (tile rows of 256, K-major; the last column tile's maps
 // have boxes of ncl rows).
-// Warp roles: warp 0 streams the four pieces of each 32-wide reduction block through a
-// four-stage ring (TMA, per-CTA loads); warp 1 issues 6 MMAs per block (3 products x 2
-// K-steps) into one of two tensor-memory accumulators (256 columns each), so the MMAs of
-// the next tile run while warps 2..5 drain the previous one; the epilogue warps read their
-// 32-lane quarter of the accumulator (thread = row (b, q)), form the shift sums over the
-// offsets with shuffles inside each sample's 8-lane group, and add them into gz.
+// Warp roles: warp 0 streams the pieces of each 32-wide reduction block (A of the item's
+// one or two sample tiles, B) through a four-stage ring (TMA, per-CTA loads); warp 1 issues
+// 6 MMAs per block and sample tile (3 products x 2 K-steps) into one of two tensor-memory
+// accumulators (256 columns each; a paired item's second tile at column 128), so the MMAs
+// of the next item run while warps 2..5 drain the previous one; the epilogue warps read
+// their 32-lane quarter of the accumulator (thread = row (b, q)), form the shift sums over
+// the offsets with shuffles inside each sample's 8-lane group, and add them into gz.
 template <int KP1>
 __global__ void __launch_bounds__(kGzThreads, 1)
     k_chunk_gz(const __grid_constant__ CUtensorMap mahi, const __grid_constant__ CUtensorMap malo,
