@@ -111,19 +111,28 @@ class TriangleSpike:
 # ----------------------------------------------------------------------------------
 
 class OracleLIF:
-    """Single-step LIF neuron with explicit state ``v`` (a float until the first step)."""
+    """Single-step LIF neuron with explicit state ``v`` (a float until the first step).
+
+    The membrane starts at v_reset (0 for the soft reset), as SpikingJelly's LIFNode and
+    the reference's v2 scans have it.  ``v_init`` overrides that start: the reference's
+    Triton kernels begin every scan at 0 (recdel_base.py:53, the same in the synaptic
+    kernels), which differs from v2 only for a hard reset to a nonzero value."""
 
     def __init__(self, tau=2.0, v_threshold=1.0, v_reset=0.0, surrogate=None,
-                 detach_reset=False):
+                 detach_reset=False, v_init=None):
         self.tau = float(tau)
         self.v_threshold = float(v_threshold)
         self.v_reset = None if v_reset is None else float(v_reset)
         self.surrogate = surrogate if surrogate is not None else ATanSpike(2.0)
         self.detach_reset = bool(detach_reset)
+        self.v_init = None if v_init is None else float(v_init)
         self.reset()
 
     def reset(self):
-        self.v = 0.0 if self.v_reset is None else self.v_reset
+        if self.v_init is not None:
+            self.v = self.v_init
+        else:
+            self.v = 0.0 if self.v_reset is None else self.v_reset
 
     def single_step_forward(self, a):
         if not torch.is_tensor(self.v):

@@ -3,6 +3,9 @@
 Run here (it needs the read-only reference checkout; the GPU box never runs it):
 
     python tests/golden/make_golden.py <path of the reference checkout> [--hard-only]
+                                       [--only NAME[,NAME...]]
+
+(``--only`` regenerates the named cases of CASES and nothing else.)
 
 For every case it runs, on identical seeded inputs,
   * the reference's canonical pure-PyTorch scans ``multi_step_forward_v2``
@@ -333,6 +336,10 @@ CASES = [
     ("hyb_basic", "hybrid", 8, 12, 3, 8, 0.0, False, False, False, 4.0, 3, 2.0, 0.0, "atan", False),
     ("hyb_sigma_bias", "hybrid", 9, 16, 4, 24, 0.5, False, True, False, 6.0, 4, 2.0, 0.0, "atan", False),
     ("hyb_soft_drop", "hybrid", 10, 14, 3, 17, 0.0, False, False, True, 5.0, 2, 2.0, None, "atan", False),
+    # hard reset to a nonzero value: charge v - (v - v_reset)/tau + a, membrane starts at v_reset
+    ("ax_vreset", "axonal", 15, 14, 4, 12, 0.5, False, True, False, 5.0, 0, 2.0, -0.5, "atan", False),
+    ("syn_vreset", "synaptic", 16, 12, 3, 10, 0.5, False, False, False, 5.0, 0, 2.0, 0.3, "triangle", False),
+    ("hyb_vreset", "hybrid", 17, 14, 3, 12, 0.0, False, True, False, 5.0, 3, 3.0, -0.5, "atan", True),
 ]
 
 
@@ -368,8 +375,11 @@ def main():
     if "--hard-only" in sys.argv:
         make_hard()
         return
+    only = sys.argv[sys.argv.index("--only") + 1].split(",") if "--only" in sys.argv else None
     for (name, kind, seed, T, B, N, sigma, sigp, bias, drop, dmax, K, tau, vr, surr,
          det) in CASES:
+        if only is not None and name not in only:
+            continue
         inp = make_inputs(seed, T, B, N, kind, sigma, sigp, bias, drop, dmax, K)
         v2 = run_v2(kind, inp, sigma, sigp, tau, vr, surr, det)
         if kind == "axonal":
@@ -385,6 +395,8 @@ def main():
                  for k in ("dx", "dW", "dd") if k in tri)
         print(f"{name:16s} L-case ok: spikes v2 vs triton differ at {ydiff}, "
               f"max rel grad diff {gd:.2e}", flush=True)
+    if only is not None:
+        return
 
     # closed-form hybrid delay gradient at integer / support-edge delays, through the
     # reference's fused kernel (tests/check_hybrid_kernel.py:131-154 values)

@@ -31,10 +31,17 @@ def surrogate(meta):
     return O.ATanSpike(2.0) if meta["surr"] == "atan" else O.TriangleSpike(1.0)
 
 
-def oracle_run(case, dtype=torch.float32, device="cpu"):
+def nonzero_hard_reset(meta):
+    """A hard reset to a nonzero value: there the reference's Triton kernels start the
+    membrane at 0 and its v2 scans (SpikingJelly) at v_reset; this library follows v2."""
+    return meta["v_reset"] is not None and meta["v_reset"] != 0.0
+
+
+def oracle_run(case, dtype=torch.float32, device="cpu", v_init=None):
     """Forward + BPTT of one golden case through the oracle; returns a dict like the
     fixture's ``v2`` entry (tensors on the CPU).  ``device``/``dtype`` choose where and in
-    which precision the oracle's torch code is evaluated."""
+    which precision the oracle's torch code is evaluated; ``v_init`` the initial membrane
+    (default v_reset)."""
     if case["meta"].get("mode", 0):
         return oracle_run_hard(case, dtype, device)
     meta, inp = case["meta"], case["inputs"]
@@ -47,7 +54,7 @@ def oracle_run(case, dtype=torch.float32, device="cpu"):
     if b is not None:
         b.requires_grad_(True)
     lif = O.OracleLIF(tau=meta["tau"], v_threshold=1.0, v_reset=meta["v_reset"],
-                      surrogate=surrogate(meta), detach_reset=meta["detach_reset"])
+                      surrogate=surrogate(meta), detach_reset=meta["detach_reset"], v_init=v_init)
     kw = dict(sigma=meta["sigma"], p_spread=p, use_sig_p=meta["use_sig_p"], bias=b,
               keep=c(inp["keep"]), record_u=True)
     if meta["kind"] == "axonal":

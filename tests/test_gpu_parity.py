@@ -8,7 +8,7 @@ mirror the reference's) and checks spikes, membranes and gradients against
 import pytest
 import torch
 
-from golden_cases import case_names, load, oracle_run
+from golden_cases import case_names, load, nonzero_hard_reset, oracle_run
 from gpu_cases import check_case, layer_ns, run_cuda
 from parity import compare_grads, compare_scan, rel_err
 from oracle import delrec_oracle as O
@@ -31,7 +31,9 @@ def test_golden_case(name):
     case = load(name)
     meta = case["meta"]
     got = run_cuda(meta, case["inputs"])
-    for ref_name in ("v2", "triton"):
+    # a nonzero hard reset: the membrane starts at v_reset here and in the reference's v2
+    # scans, at 0 in its Triton kernels (the CPU oracle tests pin that difference)
+    for ref_name in ("v2",) if nonzero_hard_reset(meta) else ("v2", "triton"):
         ref = case[ref_name]
         ties, clean = compare_scan(got["y"], got["u"], ref["y"], ref["u"])
         assert clean, f"{ties} near-ties against the reference {ref_name}"
