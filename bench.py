@@ -648,13 +648,17 @@ def roofline_probe(model, step, x, labels, spec, B):
            "traffic_source": "ncu dram bytes per sample-timestep of a T=64 capture of the same kernels "
                              "(profiles/), scaled to B*T" if per_unit else None}
     if chunked:
-        # the chunk GEMMs: executed tensor-core work (every tile's 128x256 MMAs, three bf16
-        # products over the N-target reduction) against the measured sustained bf16 rate
+        # the chunk GEMMs: executed tensor-core work (128-row tiles, 256 columns wide except
+        # the last column block's, which is its used columns rounded up to 16; three bf16
+        # products over the N-target reduction in blocks of 32) against the measured
+        # sustained bf16 rate
         K = spec["offsets"] + 1
         ntg = (256 // K) & ~3
-        tiles = math.ceil(B / 16) * math.ceil(N / ntg)
+        ntiles = math.ceil(N / ntg)
+        ncl = min(256, ((N - (ntiles - 1) * ntg) * K + 15) // 16 * 16)
+        cols = math.ceil(B / 16) * ((ntiles - 1) * 256 + ncl)
         nchunks = math.ceil(T / 8)
-        exec_flops = tiles * 2.0 * 128 * 256 * (math.ceil(N / 64) * 64) * 3 * nchunks
+        exec_flops = cols * 2.0 * 128 * (math.ceil(N / 32) * 32) * 3 * nchunks
         layers = n
         g_ms = gemm_ms / layers
         out["chunk_gemm"] = {"kernel": "k_chunk_gz", "ms_per_layer": g_ms, "launches_per_layer": n_gemm / layers,
