@@ -602,6 +602,18 @@ def _profiled_traffic(kernel):
     return None
 
 
+def chunk_gemm_executed_flops(B, N, T, KP1):
+    """Tensor-core flops the chunk GEMMs (k_chunk_gz) of one layer's reverse scan execute:
+    per chunk of 8 steps, 128-row tiles (16 samples) x (source, offset) columns -- 256 per
+    full column block of (256 // KP1) & ~3 sources, the last block its used columns rounded
+    up to 16 -- over the N-target reduction padded to blocks of 32, three bf16 products."""
+    ntg = (256 // KP1) & ~3
+    ntiles = math.ceil(N / ntg)
+    ncl = min(256, ((N - (ntiles - 1) * ntg) * KP1 + 15) // 16 * 16)
+    cols = math.ceil(B / 16) * ((ntiles - 1) * 256 + ncl)
+    return cols * 2.0 * 128 * (math.ceil(N / 32) * 32) * 3 * math.ceil(T / 8)
+
+
 def roofline_probe(model, step, x, labels, spec, B):
     """Average duration of the reverse-scan kernel (the dominant kernel of the step) over
     the launches of two training steps, timed with CUDA events recorded on the stream
@@ -648,17 +660,8 @@ def roofline_probe(model, step, x, labels, spec, B):
            "traffic_source": "ncu dram bytes per sample-timestep of a T=64 capture of the same kernels "
                              "(profiles/), scaled to B*T" if per_unit else None}
     if chunked:
-        # the chunk GEMMs: executed tensor-core work (128-row tiles, 256 columns wide except
-        # the last column block's, which is its used columns rounded up to 16; three bf16
-        # products over the N-target reduction in blocks of 32) against the measured
-        # sustained bf16 rate
-        K = spec["offsets"] + 1
-        ntg = (256 // K) & ~3
-        ntiles = math.ceil(N / ntg)
-        ncl = min(256, ((N - (ntiles - 1) * ntg) * K + 15) // 16 * 16)
-        cols = math.ceil(B / 16) * ((ntiles - 1) * 256 + ncl)
-        nchunks = math.ceil(T / 8)
-        exec_flops = cols * 2.0 * 128 * (math.ceil(N / 32) * 32) * 3 * nchunks
+        # the chunk GEMMs: executed tensor-core work against the measured sustained bf16 rate
+        exec_flops = chunk_gemm_executed_flops(B, N, T, spec["offsets"] + 1)
         layers = n
         g_ms = gemm_ms / layers
         out["chunk_gemm"] = {"kernel": "k_chunk_gz", "ms_per_layer": g_ms, "launches_per_layer": n_gemm / layers,
