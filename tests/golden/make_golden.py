@@ -292,15 +292,18 @@ def run_triton_synaptic(kind, inp, sigma, use_sig_p, tau, v_reset, surr, detach_
         M = T - l
         C[:, :, l] = gr[l:T].reshape(M * B, N).t() @ y[0:M].reshape(M * B, N)
     out["dW"] = (mask3.detach() * C).sum(-1)
-    if kind == "hybrid":
+    if kind == "hybrid" and not use_sig_p:
         dd_full = ref_delay_grad(C, W, d, sigma, Lm)
         out["dd_full"] = dd_full
         out["dd"] = dd_full.sum(0)          # the parametrization's broadcast-add backward
     else:
+        # the event-driven Function's reductions; a hybrid layer with use_sig_p takes this
+        # path too, because the hybrid kernel refuses per-source widths
+        # (synaptic_hybrid.py:56, 140) and synaptic_recdel.forward falls back to it
         targets = [d_] + ([p_] if use_sig_p else [])
         grads = torch.autograd.grad(mask3, targets, grad_outputs=W.unsqueeze(-1) * C,
                                     allow_unused=True)
-        out["dd"] = grads[0]
+        out["dd"] = grads[0].sum(0) if kind == "hybrid" else grads[0]
         if use_sig_p:
             out["dp"] = grads[1]
     return out
@@ -340,6 +343,8 @@ CASES = [
     ("ax_vreset", "axonal", 15, 14, 4, 12, 0.5, False, True, False, 5.0, 0, 2.0, -0.5, "atan", False),
     ("syn_vreset", "synaptic", 16, 12, 3, 10, 0.5, False, False, False, 5.0, 0, 2.0, 0.3, "triangle", False),
     ("hyb_vreset", "hybrid", 17, 14, 3, 12, 0.0, False, True, False, 5.0, 3, 3.0, -0.5, "atan", True),
+    # per-source triangle widths (use_sig_p) on the hybrid layer
+    ("hyb_sigp", "hybrid", 18, 12, 3, 14, 1.0, True, True, False, 5.0, 3, 2.0, 0.0, "triangle", False),
 ]
 
 

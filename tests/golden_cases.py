@@ -11,10 +11,17 @@ from oracle import delrec_oracle as O
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
 
-def case_names():
+# Fixtures that pin the oracle on the CPU but have not yet run through the library on a
+# GPU: the hybrid kernels' route with per-source widths (use_sig_p with the base window at
+# most one lag below lag 1; the random GPU case with use_sig_p takes the per-synapse route).
+NOT_YET_ON_GPU = ("hyb_sigp",)
+
+
+def case_names(gpu=False):
     other = ("hybrid_dd", "ax_hard", "ref_state_dicts")   # fixtures of other tests
-    return sorted(os.path.basename(p)[:-3] for p in glob.glob(os.path.join(GOLDEN, "*.pt"))
-                  if not os.path.basename(p).startswith(other))
+    names = sorted(os.path.basename(p)[:-3] for p in glob.glob(os.path.join(GOLDEN, "*.pt"))
+                   if not os.path.basename(p).startswith(other))
+    return [n for n in names if not (gpu and n in NOT_YET_ON_GPU)]
 
 
 def hard_cases():

@@ -26,7 +26,7 @@ def _fn():
 _layer_ns = layer_ns
 
 
-@pytest.mark.parametrize("name", case_names())
+@pytest.mark.parametrize("name", case_names(gpu=True))
 def test_golden_case(name):
     case = load(name)
     meta = case["meta"]
